@@ -1,0 +1,439 @@
+"""Benchmark: batched n=4 Birkhoff projection, forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...     (one rank per GPU)
+
+One step is one pass of the hot path over one batch: the Newton forward
+(mhc_proj.torch.birkhoff_proj_n4, tol 1e-6) then the implicit-function-theorem
+backward (mhc_proj.torch.birkhoff_proj_n4_backward) on 2^24 matrices per GPU
+with logits x ~ N(0,1) and upstream gradient G ~ N(0,1) (seeded synthetic
+inputs of the workload's shape and distribution).  The batch is sharded
+across GPUs with no collective on the data path, so per-GPU work is fixed as
+N grows (weak scaling); the value is the whole job's matrices per second over
+the slowest rank's device time.
+
+Printed (rank 0): one JSON line with the metric, the roofline of the dominant
+kernel, the end-to-end number through the public API with host buffers, the
+CPU baseline (the oracle's C port on the host's cores) and the SM clocks seen
+during the timed region.
+
+`--impl reference` times the reference algorithm on the host CPU instead (the
+reference's only CPU implementation of this path is its algorithm itself; the
+C port in oracle/ runs it on every host thread) and prints the same line with
+"impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "mhc-proj_b200")]
+
+METRIC = "fwd+bwd matrices/s and % HBM roofline at N=2^24 fp32, 1/2/4/8 B200"
+UNIT = "matrices/s"
+BYTES_FWD = 128      # R in (64 B) + T out (64 B) per matrix
+BYTES_BWD = 192      # G, T in + D out per matrix
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=1 << 24, help="matrices per GPU")
+    ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
+    ap.add_argument("--tol", type=float, default=1e-6)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return world, rank, local
+
+
+def measured_peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic_per_matrix():
+    """DRAM bytes per matrix of the forward kernel from the committed ncu
+    summary (profiles/roofline_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["forward"]["dram_bytes_per_matrix"])
+    except Exception:
+        return None
+
+
+def workload_config(args, world):
+    return {
+        "workload": f"Newton forward (tol {args.tol:g}) + IFT backward, N=2^{args.n.bit_length() - 1} fp32 4x4 "
+                    f"per GPU, x~{args.dist}, G~N(0,1)",
+        "n_per_gpu": args.n,
+        "global_batch": args.n * world,
+        "tol": args.tol,
+        "distribution": args.dist,
+        "seed": 0,
+        "parallelism": f"dp{world} (batch-sharded, no collective)",
+        "l2": "inputs larger than L2 (1 GiB per tensor vs 126 MB); no flush needed",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        if not getattr(self, "lines", None):
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        top = max(sm)
+        loaded = [v for v in sm if v >= 0.5 * top] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (the oracle's C port; vanilla PyTorch Sinkhorn)
+# ---------------------------------------------------------------------------
+def cpu_port_rate(seconds: float, chunk: int, dist: str, tol: float, threads: int = 0):
+    """Newton fwd + IFT bwd with the C port of the reference algorithm on
+    `threads` host threads (0 = all), on chunks of synthetic inputs until
+    `seconds` have passed.  Returns (matrices/s, threads, matrices done)."""
+    import numpy as np
+
+    import oracle
+
+    nt = threads or oracle.max_threads()
+    rng = np.random.default_rng(0)
+    R = rng.standard_normal((chunk, 4, 4), dtype=np.float32)
+    if dist != "normal":
+        R *= rng.uniform(0.5, 4.0, size=(chunk, 1, 1)).astype(np.float32)
+    G = rng.standard_normal((chunk, 4, 4), dtype=np.float32)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        T = oracle.birkhoff_proj_n4(R, tol, threads=nt)
+        oracle.birkhoff_proj_n4_backward(G, T, threads=nt)
+        done += chunk
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return done / el, nt, done
+
+
+def vanilla_sk_cpu_rate(reps: int = 10):
+    """The reference's vanilla PyTorch SK20 (README.md:37-46) forward +
+    autograd backward on the host, N = 4096, all threads."""
+    import torch
+
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(123)
+    x = torch.randn(4096, 4, 4, generator=g)
+    G = torch.randn(4096, 4, 4, generator=g)
+    oracle.vanilla_sinkhorn(x, G)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.vanilla_sinkhorn(x, G)
+    el = (time.perf_counter() - t0) / reps
+    return {"value": 4096 / el, "unit": UNIT, "cores": torch.get_num_threads(),
+            "sample": "vanilla PyTorch SK20 (eps 1e-6) fwd + autograd bwd, N=4096 x~N(0,1) seed 123, eager"}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the algorithm on the host CPU
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import oracle
+
+    nt = oracle.max_threads()
+    chunk = 1 << 18
+    rng = np.random.default_rng(0)
+    R = rng.standard_normal((chunk, 4, 4), dtype=np.float32)
+    G = rng.standard_normal((chunk, 4, 4), dtype=np.float32)
+
+    def step():
+        T = oracle.birkhoff_proj_n4(R, args.tol, threads=nt)
+        oracle.birkhoff_proj_n4_backward(G, T, threads=nt)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = chunk * args.steps / el
+    sample = (f"{chunk} matrices per step (x~N(0,1), G~N(0,1)) of the N=2^24 workload: Newton fwd + IFT bwd, "
+              f"C port of the reference algorithm, {nt} pthreads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": nt, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+
+    import mhc_proj  # fails loudly without the native extension
+
+    from mhc_proj.workloads import make_logits
+
+    n = args.n
+    proj = mhc_proj.torch.birkhoff_proj_n4
+    proj_bwd = mhc_proj.torch.birkhoff_proj_n4_backward
+    R = make_logits(args.dist, n, seed=1000 + rank, device=dev)
+    G = make_logits("normal", n, seed=2000 + rank, device=dev)
+    tol = args.tol
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record()
+        T = proj(R, tol)["T"]
+        if ev is not None:
+            ev[1].record()
+        D = proj_bwd(G, T)["D"]
+        if ev is not None:
+            ev[2].record()
+        return T, D
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for i in range(args.steps):
+            step(evs[i])
+        t_end.record()
+        barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+
+    # end to end through the public API with host buffers: pinned inputs go
+    # up, T and D come back, chunks pipelined over two streams
+    e2e = run_e2e(args, R, G, dev, world)
+
+    stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    total_ms, fwd_ms, bwd_ms, e2e_ms = stats.tolist()
+    ms_per_step = total_ms / args.steps
+
+    if rank == 0:
+        peak, peak_kind = measured_peak_hbm()
+        fwd_gbs = BYTES_FWD * n / (fwd_ms * 1e-3) / 1e9
+        bwd_gbs = BYTES_BWD * n / (bwd_ms * 1e-3) / 1e9
+        step_gbs = (BYTES_FWD + BYTES_BWD) * n / (ms_per_step * 1e-3) / 1e9
+        tpm = ncu_traffic_per_matrix()
+        line = {
+            "metric": METRIC,
+            "value": world * n / (ms_per_step * 1e-3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded torch generators; workload shape and distribution)",
+            "config": workload_config(args, world),
+            "roofline": {
+                "bound": "hbm", "kernel": "birkhoff_fwd_kernel (Newton forward)",
+                "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_matrix": BYTES_FWD,
+                "traffic": None if tpm is None else tpm * n,
+                "step": {"achieved": step_gbs, "frac": step_gbs / peak,
+                         "algorithmic_bytes_per_matrix": BYTES_FWD + BYTES_BWD},
+                "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms,
+                            "forward_gbs": fwd_gbs, "backward_gbs": bwd_gbs,
+                            "backward_frac": bwd_gbs / peak},
+            },
+            "e2e": {"value": world * n / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "ms_per_step": e2e_ms, "how": e2e["how"]},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            rate, nt, done = cpu_port_rate(args.cpu_seconds, 1 << 18, args.dist, tol)
+            line["cpu_baseline"] = {
+                "value": rate, "unit": UNIT, "cores": nt, "kind": "port",
+                "sample": f"{done} matrices in chunks of 2^18 (same distribution): Newton fwd + IFT bwd, "
+                          f"C port of the reference algorithm in oracle/, {nt} pthreads",
+                "vanilla_sk20_torch_cpu": vanilla_sk_cpu_rate(),
+            }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, R, G, dev, world):
+    """End to end through mhc_proj.torch.* with host buffers: each step copies
+    R and G from pinned host memory, runs the forward and backward, and copies
+    T and D back to pinned host memory; the batch moves in chunks over two
+    streams so copies in both directions overlap the kernels."""
+    import torch
+
+    import mhc_proj
+
+    n = R.shape[0]
+    chunks = 8 if n >= (1 << 20) else 1
+    Rh = R.cpu().pin_memory()
+    Gh = G.cpu().pin_memory()
+    Th = torch.empty_like(Rh).pin_memory()
+    Dh = torch.empty_like(Rh).pin_memory()
+    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    bounds = [(n * i // chunks, n * (i + 1) // chunks) for i in range(chunks)]
+    tol = args.tol
+
+    def step():
+        for i, (a, b) in enumerate(bounds):
+            s = streams[i % 2]
+            with torch.cuda.stream(s):
+                r = Rh[a:b].to(dev, non_blocking=True)
+                g = Gh[a:b].to(dev, non_blocking=True)
+                T = mhc_proj.torch.birkhoff_proj_n4(r, tol)["T"]
+                D = mhc_proj.torch.birkhoff_proj_n4_backward(g, T)["D"]
+                Th[a:b].copy_(T, non_blocking=True)
+                Dh[a:b].copy_(D, non_blocking=True)
+                for t in (r, g, T, D):
+                    t.record_stream(s)
+        for s in streams:
+            torch.cuda.current_stream(dev).wait_stream(s)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[dev.index])
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.e2e_steps
+    nbytes = n * 64
+    return {"ms": ms, "h2d": 2 * nbytes, "d2h": 2 * nbytes,
+            "how": f"pinned host R,G -> device -> fwd+bwd (public API) -> T,D to pinned host; "
+                   f"{chunks} chunks over 2 streams; {args.e2e_steps} steps timed with CUDA events"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,87 @@
+/*
+ * mhc_proj -- batched n=4 Birkhoff projection on B200 (sm_100a).
+ *
+ * C ABI of libmhcproj.so.  Every entry point takes device pointers to N
+ * contiguous row-major 4x4 fp32 matrices (64 bytes each), launches on
+ * `stream` and returns without synchronising.  Pointers that are 16-byte
+ * aligned take the 128-bit load/store path; any other alignment is accepted
+ * and served by a scalar path.  Inputs and outputs must not overlap.
+ *
+ * Return value: MHC_OK (0), a negative MHC_ERR_* code for a rejected argument
+ * (nothing is launched), or a positive cudaError_t from the launch.
+ *
+ * These entry points replace the reference's C++ launchers, which return
+ * void and check nothing; each declaration cites the one it replaces
+ * (file:line in the reference project).
+ */
+#ifndef MHC_PROJ_H
+#define MHC_PROJ_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MHC_PROJ_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MHC_API __attribute__((visibility("default")))
+#else
+#define MHC_API
+#endif
+
+enum {
+    MHC_OK = 0,
+    MHC_ERR_INVALID_VALUE = -1, /* N < 0, or a null pointer with N > 0 */
+    MHC_ERR_ITERS = -2          /* iteration count outside the supported range */
+};
+
+/* Largest iteration count sinkhorn_knopp_n4_backward accepts (the
+ * reference's limit, src/sinkhorn_knopp.cuh:1213). */
+#define MHC_SK_BACKWARD_MAX_ITERS 20
+
+/* Forward KL projection by dual Newton: T = diag(e^a) exp(R) diag(e^b) with
+ * unit row sums and column sums within `tol` (l1 over the first three
+ * columns), at most 20 Newton iterations.
+ * Replaces: void birkhoff_proj_n4(const float* d_R, float* d_T, float tol,
+ *           int N, cudaStream_t) -- src/birkhoff_proj_n4.cu:505 */
+MHC_API int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N,
+                         cudaStream_t stream);
+
+/* Backward by the implicit function theorem: D = dL/dR given G = dL/dT and
+ * the forward output T.
+ * Replaces: void birkhoff_proj_n4_backward(const float* d_G, const float* d_T,
+ *           float* d_D, int N, cudaStream_t) -- src/birkhoff_proj_n4.cu:675 */
+MHC_API int mhc_birkhoff_proj_n4_backward(const float* d_G, const float* d_T, float* d_D,
+                                  int64_t N, cudaStream_t stream);
+
+/* Fixed-iteration Sinkhorn-Knopp on M (= exp(R)): `num_iters` row then
+ * column normalisations, a sum s <= 1e-8 giving a zero factor.
+ * num_iters <= 0 copies M to T.
+ * Replaces: void sinkhorn_knopp_n4(const float* d_M, float* d_T, int N,
+ *           int num_iters, cudaStream_t) -- src/sinkhorn_knopp_n4.cu:5 */
+MHC_API int mhc_sinkhorn_knopp_n4(const float* d_M, float* d_T, int64_t N, int num_iters,
+                          cudaStream_t stream);
+
+/* Exact gradient of sum(G .* sinkhorn_knopp_n4(M)) with respect to M.
+ * num_iters <= 0 copies G to D; num_iters > MHC_SK_BACKWARD_MAX_ITERS
+ * returns MHC_ERR_ITERS.
+ * Replaces: void sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M,
+ *           float* d_D, int N, int num_iters, cudaStream_t)
+ *           -- src/sinkhorn_knopp_n4.cu:13 */
+MHC_API int mhc_sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M, float* d_D,
+                                   int64_t N, int num_iters, cudaStream_t stream);
+
+/* Human-readable text for a return code of the functions above. */
+MHC_API const char* mhc_status_string(int status);
+
+/* MHC_PROJ_ABI_VERSION of the loaded library. */
+MHC_API int mhc_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHC_PROJ_H */

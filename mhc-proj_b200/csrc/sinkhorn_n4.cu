@@ -1,0 +1,119 @@
+// Kernels and C-ABI launchers for the fixed-iteration Sinkhorn-Knopp pair.
+#include <utility>
+
+#include "sinkhorn_n4.cuh"
+#include "mhc_proj.h"
+
+namespace mhcp {
+
+constexpr float kSkEps = 1e-8f;  // src/sinkhorn_knopp_n4.cu:10,18
+constexpr int kSkBlock = 128;
+
+template <bool kVec>
+__global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(const float* __restrict__ M, float* __restrict__ T,
+                                                          int64_t N, int iters)
+{
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= N) return;
+    Mat4 x;
+    load_mat<kVec>(M, idx, x);
+#pragma unroll 1
+    for (int it = 0; it < iters; ++it) sk_iteration(x.m, kSkEps, nullptr, nullptr, nullptr);
+    store_mat<kVec>(T, idx, x);
+}
+
+// Backward with a compile-time iteration count.  Segment starts are kept in
+// shared memory, [segment][element][thread] so that a warp's accesses fall in
+// distinct banks; each segment is then replayed in registers and reversed.
+template <int kIters, bool kVec>
+__global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restrict__ G,
+                                                          const float* __restrict__ M,
+                                                          float* __restrict__ D, int64_t N)
+{
+    constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
+    __shared__ float ckpt[kNumSeg > 0 ? kNumSeg : 1][16][kSkBlock];
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= N) return;
+    const int tid = threadIdx.x;
+
+    Mat4 x;
+    load_mat<kVec>(M, idx, x);
+#pragma unroll
+    for (int s = 0; s < kNumSeg; ++s) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ckpt[s][e][tid] = x.m[e];
+        if (s + 1 < kNumSeg) {
+#pragma unroll
+            for (int k = 0; k < kSkSeg; ++k) sk_iteration(x.m, kSkEps, nullptr, nullptr, nullptr);
+        }
+    }
+
+    Mat4 dy;
+    load_mat<kVec>(G, idx, dy);
+#pragma unroll
+    for (int s = kNumSeg - 1; s >= 0; --s) {
+        constexpr int kFull = kSkSeg;
+        const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kFull;
+        float xr[kSkSeg][16], ri[kSkSeg][4], ci[kSkSeg][4];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) x.m[e] = ckpt[s][e][tid];
+#pragma unroll
+        for (int k = 0; k < kSkSeg; ++k)
+            if (k < len) sk_iteration(x.m, kSkEps, xr[k], ri[k], ci[k]);
+#pragma unroll
+        for (int k = kSkSeg - 1; k >= 0; --k)
+            if (k < len) sk_iteration_vjp(dy.m, xr[k], ri[k], ci[k]);
+    }
+    store_mat<kVec>(D, idx, dy);
+}
+
+template <int kIters>
+static void launch_sk_bwd(bool vec, const float* G, const float* M, float* D, int64_t N, cudaStream_t stream)
+{
+    const int64_t grid = ceil_div(N, kSkBlock);
+    if (vec)
+        sk_bwd_kernel<kIters, true><<<grid, kSkBlock, 0, stream>>>(G, M, D, N);
+    else
+        sk_bwd_kernel<kIters, false><<<grid, kSkBlock, 0, stream>>>(G, M, D, N);
+}
+
+template <int... Is>
+static void dispatch_sk_bwd(int iters, bool vec, const float* G, const float* M, float* D, int64_t N,
+                            cudaStream_t stream, std::integer_sequence<int, Is...>)
+{
+    ((iters == Is + 1 ? launch_sk_bwd<Is + 1>(vec, G, M, D, N, stream) : void()), ...);
+}
+
+}  // namespace mhcp
+
+using namespace mhcp;
+
+extern "C" int mhc_sinkhorn_knopp_n4(const float* d_M, float* d_T, int64_t N, int num_iters, cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_M || !d_T))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    const int iters = num_iters > 0 ? num_iters : 0;
+    const int64_t grid = ceil_div(N, kSkBlock);
+    if (aligned16(d_M) && aligned16(d_T))
+        sk_fwd_kernel<true><<<grid, kSkBlock, 0, stream>>>(d_M, d_T, N, iters);
+    else
+        sk_fwd_kernel<false><<<grid, kSkBlock, 0, stream>>>(d_M, d_T, N, iters);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M, float* d_D, int64_t N,
+                                              int num_iters, cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_G || !d_M || !d_D))) return MHC_ERR_INVALID_VALUE;
+    if (num_iters > MHC_SK_BACKWARD_MAX_ITERS) return MHC_ERR_ITERS;
+    if (N == 0) return MHC_OK;
+    if (num_iters <= 0) {
+        const cudaError_t e = cudaMemcpyAsync(d_D, d_G, static_cast<size_t>(N) * 16 * sizeof(float),
+                                              cudaMemcpyDeviceToDevice, stream);
+        return static_cast<int>(e);
+    }
+    const bool vec = aligned16(d_G) && aligned16(d_M) && aligned16(d_D);
+    dispatch_sk_bwd(num_iters, vec, d_G, d_M, d_D, N, stream,
+                    std::make_integer_sequence<int, MHC_SK_BACKWARD_MAX_ITERS>{});
+    return static_cast<int>(cudaGetLastError());
+}

@@ -1,0 +1,150 @@
+// mhc_proj._internal: the PyTorch face of libmhcproj.so.
+//
+// Mirrors the reference's pybind11 module (src/bindings.cpp:40-60) and its
+// tensor wrappers (src/solvers_torch.cpp): a submodule `torch` with four
+// functions of the same names, argument names and defaults, each returning a
+// dict.  The conventions are the reference's:
+//   - inputs must be 3-D B x 4 x 4, else RuntimeError;
+//   - inputs of any dtype/device are converted to fp32 on the CUDA device they
+//     are on (the current CUDA device for CPU tensors) and made contiguous;
+//   - outputs are new tensors converted back to the (first) input's
+//     dtype/device; the backward converts T to G's dtype/device;
+//   - sinkhorn_knopp_n4_backward with max_iter > 20 raises ValueError;
+//   - extra keyword arguments are accepted and ignored.
+// Differences: kernels run on PyTorch's current stream of the target device
+// (the reference uses cudaStreamPerThread), batch sizes are 64-bit, B = 0 is
+// a no-op, and a failed launch raises RuntimeError.
+#include <stdexcept>
+#include <string>
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <pybind11/pybind11.h>
+#include <torch/extension.h>
+
+#include "mhc_proj.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check_batch(const torch::Tensor& x, const char* name, int64_t batch = -1)
+{
+    const std::string msg = std::string(name) + " must be a tensor of size B x 4 x 4";
+    if (x.dim() != 3) throw std::runtime_error(msg);
+    if (x.size(1) != 4 || x.size(2) != 4) throw std::runtime_error(msg);
+    if (batch >= 0 && x.size(0) != batch) throw std::runtime_error(msg);
+}
+
+// fp32 on the tensor's own CUDA device, or on the current device for
+// non-CUDA tensors (solvers_torch.cpp:52-61).
+torch::TensorOptions target_options(const torch::Tensor& x)
+{
+    auto opts = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA);
+    if (x.device().is_cuda()) opts = opts.device(torch::kCUDA, x.device().index());
+    return opts;
+}
+
+void check_status(int status, const char* what)
+{
+    if (status != MHC_OK)
+        throw std::runtime_error(std::string(what) + " failed: " + mhc_status_string(status));
+}
+
+cudaStream_t current_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+py::dict birkhoff_proj_n4(torch::Tensor R, float tol, const py::kwargs&)
+{
+    check_batch(R, "R");
+    const auto src = R.options();
+    const auto opts = target_options(R);
+    R = R.to(opts);
+    const c10::cuda::CUDAGuard guard(R.device());
+    R = R.contiguous();
+    const int64_t n = R.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_birkhoff_proj_n4(R.data_ptr<float>(), T.data_ptr<float>(), tol, n, current_stream()),
+                 "birkhoff_proj_n4");
+    py::dict out;
+    out["T"] = T.to(src);
+    return out;
+}
+
+py::dict birkhoff_proj_n4_backward(torch::Tensor G, torch::Tensor T, const py::kwargs&)
+{
+    check_batch(G, "G");
+    check_batch(T, "T", G.size(0));
+    const auto src = G.options();
+    const auto opts = target_options(G);
+    G = G.to(opts);
+    T = T.to(opts);
+    const c10::cuda::CUDAGuard guard(G.device());
+    G = G.contiguous();
+    T = T.contiguous();
+    const int64_t n = G.size(0);
+    torch::Tensor D = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_birkhoff_proj_n4_backward(G.data_ptr<float>(), T.data_ptr<float>(), D.data_ptr<float>(), n,
+                                               current_stream()),
+                 "birkhoff_proj_n4_backward");
+    py::dict out;
+    out["D"] = D.to(src);
+    return out;
+}
+
+py::dict sinkhorn_knopp_n4(torch::Tensor M, int max_iter, const py::kwargs&)
+{
+    check_batch(M, "M");
+    const auto src = M.options();
+    const auto opts = target_options(M);
+    M = M.to(opts);
+    const c10::cuda::CUDAGuard guard(M.device());
+    M = M.contiguous();
+    const int64_t n = M.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_sinkhorn_knopp_n4(M.data_ptr<float>(), T.data_ptr<float>(), n, max_iter, current_stream()),
+                 "sinkhorn_knopp_n4");
+    py::dict out;
+    out["T"] = T.to(src);
+    return out;
+}
+
+py::dict sinkhorn_knopp_n4_backward(torch::Tensor G, torch::Tensor M, int max_iter, const py::kwargs&)
+{
+    check_batch(G, "G");
+    check_batch(M, "M", G.size(0));
+    if (max_iter > MHC_SK_BACKWARD_MAX_ITERS)
+        throw std::invalid_argument("sinkhorn_knopp_n4_backward supports max_iter <= " +
+                                    std::to_string(MHC_SK_BACKWARD_MAX_ITERS));
+    const auto src = G.options();
+    const auto opts = target_options(G);
+    G = G.to(opts);
+    M = M.to(opts);
+    const c10::cuda::CUDAGuard guard(G.device());
+    G = G.contiguous();
+    M = M.contiguous();
+    const int64_t n = G.size(0);
+    torch::Tensor D = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_sinkhorn_knopp_n4_backward(G.data_ptr<float>(), M.data_ptr<float>(), D.data_ptr<float>(), n,
+                                                max_iter, current_stream()),
+                 "sinkhorn_knopp_n4_backward");
+    py::dict out;
+    out["D"] = D.to(src);
+    return out;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_internal, m)
+{
+    m.doc() = "B200 batched n=4 Birkhoff projection for manifold-constrained hyper-connections";
+    m.attr("abi_version") = mhc_abi_version();
+    py::module m_torch = m.def_submodule("torch", "PyTorch interface");
+    m_torch.def("birkhoff_proj_n4", &birkhoff_proj_n4, py::arg("R"), py::arg("tol") = 1e-6,
+                "KL projection of 4x4 matrices onto the Birkhoff polytope");
+    m_torch.def("birkhoff_proj_n4_backward", &birkhoff_proj_n4_backward, py::arg("G"), py::arg("T"),
+                "KL projection of 4x4 matrices onto the Birkhoff polytope, backward pass");
+    m_torch.def("sinkhorn_knopp_n4", &sinkhorn_knopp_n4, py::arg("M"), py::arg("max_iter") = 20,
+                "Sinkhorn-Knopp algorithm for 4x4 matrices");
+    m_torch.def("sinkhorn_knopp_n4_backward", &sinkhorn_knopp_n4_backward, py::arg("G"), py::arg("M"),
+                py::arg("max_iter") = 20, "Sinkhorn-Knopp algorithm for 4x4 matrices, backward pass");
+}

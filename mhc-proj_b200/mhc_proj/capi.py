@@ -1,0 +1,136 @@
+"""ctypes view of the C ABI in include/mhc_proj.h (libmhcproj.so).
+
+For callers that hold raw device pointers instead of tensors.  Each function
+mirrors the C entry point; ``stream`` is a raw cudaStream_t (an int, 0 for the
+legacy default stream) and every pointer is a device address (an int).  A
+non-zero return code raises ``MhcError``.  The ``*_tensor`` helpers take
+contiguous fp32 CUDA tensors and launch on PyTorch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmhcproj.so")
+
+EXPORTED = (
+    "mhc_birkhoff_proj_n4",
+    "mhc_birkhoff_proj_n4_backward",
+    "mhc_sinkhorn_knopp_n4",
+    "mhc_sinkhorn_knopp_n4_backward",
+    "mhc_status_string",
+    "mhc_abi_version",
+)
+
+MHC_OK = 0
+MHC_ERR_INVALID_VALUE = -1
+MHC_ERR_ITERS = -2
+MHC_SK_BACKWARD_MAX_ITERS = 20
+
+
+class MhcError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        self.code = code
+        super().__init__(f"{what} failed ({code}): {status_string(code)}")
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise RuntimeError(f"{_LIB_PATH} is not built (run `python mhc-proj_b200/build.py`)")
+        L = ctypes.CDLL(_LIB_PATH)
+        vp, i64, f32, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int
+        L.mhc_birkhoff_proj_n4.argtypes = [vp, vp, f32, i64, vp]
+        L.mhc_birkhoff_proj_n4_backward.argtypes = [vp, vp, vp, i64, vp]
+        L.mhc_sinkhorn_knopp_n4.argtypes = [vp, vp, i64, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_backward.argtypes = [vp, vp, vp, i64, i32, vp]
+        for f in EXPORTED[:4]:
+            getattr(L, f).restype = ctypes.c_int
+        L.mhc_status_string.argtypes = [ctypes.c_int]
+        L.mhc_status_string.restype = ctypes.c_char_p
+        L.mhc_abi_version.argtypes = []
+        L.mhc_abi_version.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().mhc_status_string(int(code)).decode()
+
+
+def abi_version() -> int:
+    return lib().mhc_abi_version()
+
+
+def _check(code: int, what: str) -> None:
+    if code != MHC_OK:
+        raise MhcError(code, what)
+
+
+def birkhoff_proj_n4(R: int, T: int, tol: float, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4(R, T, tol, N, stream), "mhc_birkhoff_proj_n4")
+
+
+def birkhoff_proj_n4_backward(G: int, T: int, D: int, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_backward(G, T, D, N, stream), "mhc_birkhoff_proj_n4_backward")
+
+
+def sinkhorn_knopp_n4(M: int, T: int, N: int, num_iters: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4(M, T, N, num_iters, stream), "mhc_sinkhorn_knopp_n4")
+
+
+def sinkhorn_knopp_n4_backward(G: int, M: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_backward(G, M, D, N, num_iters, stream), "mhc_sinkhorn_knopp_n4_backward")
+
+
+# --- tensor conveniences ---------------------------------------------------
+
+def _dev(x, name):
+    import torch
+
+    if not (x.is_cuda and x.dtype == torch.float32 and x.is_contiguous() and x.dim() == 3
+            and tuple(x.shape[1:]) == (4, 4)):
+        raise ValueError(f"{name} must be a contiguous float32 CUDA tensor of shape (N, 4, 4)")
+    return x.data_ptr()
+
+
+def _stream(x) -> int:
+    import torch
+
+    return torch.cuda.current_stream(x.device).cuda_stream
+
+
+def birkhoff_proj_n4_tensor(R, tol: float = 1e-6, out=None):
+    import torch
+
+    T = torch.empty_like(R) if out is None else out
+    birkhoff_proj_n4(_dev(R, "R"), _dev(T, "T"), tol, R.shape[0], _stream(R))
+    return T
+
+
+def birkhoff_proj_n4_backward_tensor(G, T, out=None):
+    import torch
+
+    D = torch.empty_like(G) if out is None else out
+    birkhoff_proj_n4_backward(_dev(G, "G"), _dev(T, "T"), _dev(D, "D"), G.shape[0], _stream(G))
+    return D
+
+
+def sinkhorn_knopp_n4_tensor(M, num_iters: int = 20, out=None):
+    import torch
+
+    T = torch.empty_like(M) if out is None else out
+    sinkhorn_knopp_n4(_dev(M, "M"), _dev(T, "T"), M.shape[0], num_iters, _stream(M))
+    return T
+
+
+def sinkhorn_knopp_n4_backward_tensor(G, M, num_iters: int = 20, out=None):
+    import torch
+
+    D = torch.empty_like(G) if out is None else out
+    sinkhorn_knopp_n4_backward(_dev(G, "G"), _dev(M, "M"), _dev(D, "D"), G.shape[0], num_iters, _stream(G))
+    return D

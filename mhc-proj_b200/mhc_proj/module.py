@@ -1,0 +1,84 @@
+"""Autograd functions and modules over the native kernels.
+
+Same classes, signatures and behaviour as the reference's
+mhc_proj/module.py:5-84:
+  MHCProjectionN4(tol=1e-6)      forward: Newton projection, saves T;
+                                 backward: implicit-function-theorem kernel.
+  MHCSinkhornN4(max_iter=20)     forward: exp then fixed-iteration
+                                 Sinkhorn-Knopp, saves exp(R); backward: the
+                                 Sinkhorn-Knopp backward kernel times exp(R).
+Both take any tensor whose last two dimensions are 4 x 4 (ValueError
+otherwise) and return a tensor of the input's shape.  A ``None`` incoming
+gradient (possible because gradient materialisation is off) yields ``None``.
+"""
+import torch
+import torch.nn as nn
+
+from . import _internal
+
+
+class MHCProjectionN4Function(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, R, tol=1e-6):
+        in_shape = R.shape
+        R = R.reshape(-1, 4, 4)
+        T = _internal.torch.birkhoff_proj_n4(R, tol)["T"]
+        ctx.save_for_backward(T)
+        ctx.set_materialize_grads(False)
+        return T.view(in_shape)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if not ctx.needs_input_grad[0] or grad_output is None:
+            return None, None
+        in_shape = grad_output.shape
+        G = grad_output.reshape(-1, 4, 4)
+        (T,) = ctx.saved_tensors
+        D = _internal.torch.birkhoff_proj_n4_backward(G, T)["D"]
+        return D.view(in_shape), None
+
+
+class MHCProjectionN4(nn.Module):
+    def __init__(self, tol=1e-6):
+        super().__init__()
+        self.tol = tol
+
+    def forward(self, x):
+        in_shape = x.shape
+        if x.ndim < 2 or in_shape[-1] != 4 or in_shape[-2] != 4:
+            raise ValueError("x must be a tensor of size B x 4 x 4")
+        return MHCProjectionN4Function.apply(x, self.tol)
+
+
+class MHCSinkhornN4Function(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, R, max_iter=20):
+        in_shape = R.shape
+        expon = torch.exp(R.reshape(-1, 4, 4))
+        T = _internal.torch.sinkhorn_knopp_n4(expon, max_iter)["T"]
+        ctx.max_iter = max_iter
+        ctx.save_for_backward(expon)
+        ctx.set_materialize_grads(False)
+        return T.view(in_shape)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if not ctx.needs_input_grad[0] or grad_output is None:
+            return None, None
+        in_shape = grad_output.shape
+        G = grad_output.reshape(-1, 4, 4)
+        (expon,) = ctx.saved_tensors
+        D = _internal.torch.sinkhorn_knopp_n4_backward(G, expon, ctx.max_iter)["D"] * expon
+        return D.view(in_shape), None
+
+
+class MHCSinkhornN4(nn.Module):
+    def __init__(self, max_iter=20):
+        super().__init__()
+        self.max_iter = max_iter
+
+    def forward(self, x):
+        in_shape = x.shape
+        if x.ndim < 2 or in_shape[-1] != 4 or in_shape[-2] != 4:
+            raise ValueError("x must be a tensor of size B x 4 x 4")
+        return MHCSinkhornN4Function.apply(x, self.max_iter)

@@ -1,0 +1,166 @@
+"""ORACLE -- test infrastructure only.
+
+ctypes bindings over ``liboracle.so`` (the CPU restatement of the reference
+algorithms in ``birkhoff_oracle.c``) and over ``_ref/libmhcref.so`` (the
+reference's own CUDA kernels compiled unmodified from their source files,
+``ref_shim.cu`` giving them extern "C" names).
+
+Only the tests, the smoke check and the CPU-baseline leg of the benchmark use
+this package, always as the checker or the timed baseline, never as a product
+path.  Build both libraries with ``make -C oracle``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_LIB = os.path.join(_HERE, "liboracle.so")
+REF_LIB = os.path.join(_HERE, "_ref", "libmhcref.so")
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+_lib = None
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(ORACLE_LIB):
+            raise RuntimeError(f"{ORACLE_LIB} is not built; run `make -C oracle`")
+        lib = ctypes.CDLL(ORACLE_LIB)
+        lib.oracle_max_threads.restype = ctypes.c_int
+        lib.oracle_birkhoff_proj_n4.argtypes = [_f32p, _f32p, ctypes.c_float, ctypes.c_int64, _i32p, ctypes.c_int]
+        lib.oracle_birkhoff_proj_n4.restype = None
+        lib.oracle_birkhoff_proj_n4_backward.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int]
+        lib.oracle_birkhoff_proj_n4_backward.restype = None
+        lib.oracle_sinkhorn_knopp_n4.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int]
+        lib.oracle_sinkhorn_knopp_n4.restype = None
+        lib.oracle_sinkhorn_knopp_n4_backward.argtypes = [
+            _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int]
+        lib.oracle_sinkhorn_knopp_n4_backward.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def _as_batch(a: np.ndarray, name: str) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    if a.ndim != 3 or a.shape[1:] != (4, 4):
+        raise ValueError(f"{name} must have shape (N, 4, 4), got {a.shape}")
+    return a
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(_f32p)
+
+
+def max_threads() -> int:
+    return _load().oracle_max_threads()
+
+
+def birkhoff_proj_n4(R, tol=1e-6, threads=0, return_evals=False):
+    """Newton forward (birkhoff_proj_n4.cu:375-499). Returns T (and the
+    number of f/gradient evaluations per matrix if ``return_evals``)."""
+    R = _as_batch(R, "R")
+    N = R.shape[0]
+    T = np.empty_like(R)
+    ev = np.empty(N, dtype=np.int32) if return_evals else None
+    _load().oracle_birkhoff_proj_n4(_p(R), _p(T), float(tol), N,
+                                    ev.ctypes.data_as(_i32p) if ev is not None else None, int(threads))
+    return (T, ev) if return_evals else T
+
+
+def birkhoff_proj_n4_backward(G, T, threads=0):
+    """IFT backward (birkhoff_proj_n4.cu:527-669). Returns D."""
+    G = _as_batch(G, "G")
+    T = _as_batch(T, "T")
+    if G.shape != T.shape:
+        raise ValueError("G and T must have the same shape")
+    D = np.empty_like(G)
+    _load().oracle_birkhoff_proj_n4_backward(_p(G), _p(T), _p(D), G.shape[0], int(threads))
+    return D
+
+
+def sinkhorn_knopp_n4(M, max_iter=20, eps=1e-8, threads=0):
+    """Fixed-iteration SK on M = exp(R) (sinkhorn_knopp.cuh:831-912)."""
+    M = _as_batch(M, "M")
+    T = np.empty_like(M)
+    _load().oracle_sinkhorn_knopp_n4(_p(M), _p(T), M.shape[0], int(max_iter), float(eps), int(threads))
+    return T
+
+
+def sinkhorn_knopp_n4_backward(G, M, max_iter=20, eps=1e-8, exact=True, threads=0):
+    """Gradient w.r.t. M of sum(G * SK(M)).  ``exact=True`` is the exact VJP;
+    ``exact=False`` restates the reference kernel's reverse loop
+    (sinkhorn_knopp.cuh:1146-1202), whose row step is not the exact VJP."""
+    G = _as_batch(G, "G")
+    M = _as_batch(M, "M")
+    D = np.empty_like(G)
+    rc = _load().oracle_sinkhorn_knopp_n4_backward(_p(G), _p(M), _p(D), G.shape[0], int(max_iter),
+                                                   float(eps), 1 if exact else 0, int(threads))
+    if rc != 0:
+        raise ValueError("max_iter exceeds the oracle's capacity (64)")
+    return D
+
+
+def vanilla_sinkhorn(x, G=None, iters=20, eps=1e-6):
+    """The reference's vanilla PyTorch Sinkhorn-Knopp (README.md:37-46,
+    benchmark/accuracy.py:7-13): P = exp(x), then `iters` times
+    P /= (rowsum + eps); P /= (colsum + eps).  With G, also returns
+    d sum(G*P) / dx by autograd.  ``x`` and ``G`` are torch tensors; the
+    computation runs on their device."""
+    import torch
+
+    with torch.enable_grad():
+        xg = x.detach().clone().requires_grad_(G is not None)
+        P = torch.exp(xg)
+        for _ in range(iters):
+            P = P / (P.sum(dim=2, keepdim=True) + eps)
+            P = P / (P.sum(dim=1, keepdim=True) + eps)
+        if G is None:
+            return P.detach()
+        (P * G).sum().backward()
+        return P.detach(), xg.grad.detach()
+
+
+class RefCuda:
+    """The reference's CUDA kernels, compiled from its own sources.  Calls
+    take raw device pointers (ints) and a raw cudaStream_t (int)."""
+
+    def __init__(self, path: str = REF_LIB):
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is not built; run `make -C oracle ref` where the reference sources exist")
+        lib = ctypes.CDLL(path)
+        vp = ctypes.c_void_p
+        lib.ref_birkhoff_proj_n4.argtypes = [vp, vp, ctypes.c_float, ctypes.c_int, vp]
+        lib.ref_birkhoff_proj_n4_backward.argtypes = [vp, vp, vp, ctypes.c_int, vp]
+        lib.ref_sinkhorn_knopp_n4.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp]
+        lib.ref_sinkhorn_knopp_n4_backward.argtypes = [vp, vp, vp, ctypes.c_int, ctypes.c_int, vp]
+        for f in ("ref_birkhoff_proj_n4", "ref_birkhoff_proj_n4_backward",
+                  "ref_sinkhorn_knopp_n4", "ref_sinkhorn_knopp_n4_backward"):
+            getattr(lib, f).restype = ctypes.c_int
+        self.lib = lib
+
+    @staticmethod
+    def available(path: str = REF_LIB) -> bool:
+        return os.path.exists(path)
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise RuntimeError(f"reference {what} failed with code {rc}")
+
+    def birkhoff_proj_n4(self, R, T, tol, N, stream):
+        self._check(self.lib.ref_birkhoff_proj_n4(R, T, float(tol), int(N), stream), "birkhoff_proj_n4")
+
+    def birkhoff_proj_n4_backward(self, G, T, D, N, stream):
+        self._check(self.lib.ref_birkhoff_proj_n4_backward(G, T, D, int(N), stream), "birkhoff_proj_n4_backward")
+
+    def sinkhorn_knopp_n4(self, M, T, N, iters, stream):
+        self._check(self.lib.ref_sinkhorn_knopp_n4(M, T, int(N), int(iters), stream), "sinkhorn_knopp_n4")
+
+    def sinkhorn_knopp_n4_backward(self, G, M, D, N, iters, stream):
+        self._check(self.lib.ref_sinkhorn_knopp_n4_backward(G, M, D, int(N), int(iters), stream),
+                    "sinkhorn_knopp_n4_backward")

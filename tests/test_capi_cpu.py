@@ -1,0 +1,69 @@
+"""The C-ABI library loads, exports every entry point include/mhc_proj.h
+declares, and rejects bad arguments before touching a device (so these run
+without a GPU)."""
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from mhc_proj import capi
+
+HEADER = os.path.join(ROOT, "include", "mhc_proj.h")
+
+
+def declared_functions():
+    txt = open(HEADER).read()
+    return re.findall(r"^MHC_API\s+[\w\s\*]+?\b(mhc_\w+)\s*\(", txt, flags=re.M)
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert sorted(names) == sorted(capi.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = capi.lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings():
+    assert capi.abi_version() == 1
+    assert capi.status_string(0) == "success"
+    assert "invalid" in capi.status_string(capi.MHC_ERR_INVALID_VALUE)
+    assert "iteration" in capi.status_string(capi.MHC_ERR_ITERS)
+    assert capi.status_string(-77) == "unknown status"
+
+
+FAKE = 256  # a non-null address that is never dereferenced by these calls
+
+
+@pytest.mark.parametrize("fn,args", [
+    (capi.birkhoff_proj_n4, (FAKE, FAKE, 1e-6, -1)),
+    (capi.birkhoff_proj_n4, (0, FAKE, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_backward, (FAKE, 0, FAKE, 5)),
+    (capi.birkhoff_proj_n4_backward, (FAKE, FAKE, FAKE, -3)),
+    (capi.sinkhorn_knopp_n4, (FAKE, 0, 5, 20)),
+    (capi.sinkhorn_knopp_n4_backward, (0, FAKE, FAKE, 5, 20)),
+])
+def test_invalid_arguments_rejected(fn, args):
+    with pytest.raises(capi.MhcError) as e:
+        fn(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+
+
+def test_backward_iteration_limit():
+    with pytest.raises(capi.MhcError) as e:
+        capi.sinkhorn_knopp_n4_backward(FAKE, FAKE, FAKE, 5, capi.MHC_SK_BACKWARD_MAX_ITERS + 1)
+    assert e.value.code == capi.MHC_ERR_ITERS
+
+
+@pytest.mark.parametrize("fn,args", [
+    (capi.birkhoff_proj_n4, (0, 0, 1e-6, 0)),
+    (capi.birkhoff_proj_n4_backward, (0, 0, 0, 0)),
+    (capi.sinkhorn_knopp_n4, (0, 0, 0, 20)),
+    (capi.sinkhorn_knopp_n4_backward, (0, 0, 0, 0, 20)),
+])
+def test_empty_batch_is_a_no_op(fn, args):
+    fn(*args)  # no launch, no error

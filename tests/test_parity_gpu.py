@@ -1,0 +1,189 @@
+"""Parity of the CUDA kernels, called through the C ABI, with the reference.
+
+The reference's own CUDA kernels, compiled unmodified from its sources into
+oracle/_ref/libmhcref.so, run on the same device buffers; the Newton forward
+and the IFT backward must agree bit for bit.  The golden fixtures recorded
+from the reference (tests/golden) are checked too, as are the vanilla
+PyTorch Sinkhorn-Knopp (forward and autograd, within 1e-5) for the
+Sinkhorn-Knopp pair, and the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_cases, load_golden
+from mhc_proj.workloads import make_logits
+from mhc_proj import capi
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not oracle.RefCuda.available():
+        pytest.skip("oracle/_ref/libmhcref.so is not built (needs the reference sources)")
+    return oracle.RefCuda()
+
+
+def bitwise_equal(a, b):
+    return torch.equal(a.contiguous().view(torch.int32), b.contiguous().view(torch.int32))
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ref_forward(ref, R, tol=1e-6):
+    T = torch.empty_like(R)
+    ref.birkhoff_proj_n4(R.data_ptr(), T.data_ptr(), tol, R.shape[0], stream())
+    return T
+
+
+def ref_backward(ref, G, T):
+    D = torch.empty_like(G)
+    ref.birkhoff_proj_n4_backward(G.data_ptr(), T.data_ptr(), D.data_ptr(), G.shape[0], stream())
+    return D
+
+
+CONFIGS = [
+    ("normal", 1 << 20),        # Newton forward workload, N = 2^20, N(0,1)
+    ("sigma_mix", 2097152),     # training-shaped: 32 layers x 16 seqs x 4096 tokens
+    ("mixture", 1 << 22),       # mixture of the multi-GPU sweep
+    ("wide", 1 << 20),
+    ("uniform", 1 << 18),
+]
+
+
+@pytest.mark.parametrize("kind,n", CONFIGS)
+def test_forward_and_backward_bitwise(ref, kind, n):
+    R = make_logits(kind, n, seed=1000 + n)
+    G = make_logits("normal", n, seed=7)
+    T = capi.birkhoff_proj_n4_tensor(R)
+    Tr = ref_forward(ref, R)
+    assert bitwise_equal(T, Tr)
+    D = capi.birkhoff_proj_n4_backward_tensor(G, T)
+    Dr = ref_backward(ref, G, Tr)
+    assert bitwise_equal(D, Dr)
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 32, 33, 127, 4097, 100003])
+def test_ragged_batch_sizes(ref, n):
+    R = make_logits("sigma_mix", n, seed=n)
+    G = make_logits("normal", n, seed=n + 1)
+    T = capi.birkhoff_proj_n4_tensor(R)
+    assert bitwise_equal(T, ref_forward(ref, R))
+    assert bitwise_equal(capi.birkhoff_proj_n4_backward_tensor(G, T), ref_backward(ref, G, T))
+
+
+@pytest.mark.parametrize("offset", [1, 2, 3, 5])
+def test_unaligned_pointers(ref, offset):
+    n = 3001
+    R = make_logits("normal", n, seed=3)
+    G = make_logits("normal", n, seed=4)
+    bufs = [torch.empty(n * 16 + offset, device="cuda") for _ in range(4)]
+    Ru, Gu, Tu, Du = (b[offset:].view(n, 4, 4) for b in bufs)
+    Ru.copy_(R)
+    Gu.copy_(G)
+    capi.birkhoff_proj_n4(Ru.data_ptr(), Tu.data_ptr(), 1e-6, n, stream())
+    capi.birkhoff_proj_n4_backward(Gu.data_ptr(), Tu.data_ptr(), Du.data_ptr(), n, stream())
+    Tr = ref_forward(ref, R)
+    assert bitwise_equal(Tu, Tr)
+    assert bitwise_equal(Du, ref_backward(ref, G, Tr))
+
+
+@pytest.mark.parametrize("tol", [1e-3, 1e-5, 1e-7, 0.0, float("inf")])
+def test_tolerances(ref, tol):
+    R = make_logits("mixture", 50000, seed=11)
+    assert bitwise_equal(capi.birkhoff_proj_n4_tensor(R, tol=tol), ref_forward(ref, R, tol))
+
+
+def test_nonfinite_inputs(ref):
+    R = make_logits("normal", 4096, seed=5)
+    flat = R.view(-1)
+    flat[::97] = float("nan")
+    flat[13::89] = float("inf")
+    flat[29::83] = float("-inf")
+    flat[41::79] = 1e30
+    T = capi.birkhoff_proj_n4_tensor(R)
+    assert bitwise_equal(T, ref_forward(ref, R))
+    G = make_logits("normal", 4096, seed=6)
+    Tr = ref_forward(ref, R)
+    assert bitwise_equal(capi.birkhoff_proj_n4_backward_tensor(G, Tr), ref_backward(ref, G, Tr))
+
+
+@pytest.mark.parametrize("case", golden_cases())
+def test_golden_fixtures(case):
+    g = load_golden(case)
+    R = torch.from_numpy(g["R"]).cuda()
+    T = capi.birkhoff_proj_n4_tensor(R)
+    assert np.array_equal(T.cpu().numpy().view(np.uint32), g["T_ref"].view(np.uint32))
+    D = capi.birkhoff_proj_n4_backward_tensor(torch.from_numpy(g["G"]).cuda(), torch.from_numpy(g["T_ref"]).cuda())
+    assert np.array_equal(D.cpu().numpy().view(np.uint32), g["D_ref"].view(np.uint32))
+    Tsk = capi.sinkhorn_knopp_n4_tensor(torch.from_numpy(g["M"]).cuda(), 20)
+    assert np.array_equal(Tsk.cpu().numpy().view(np.uint32), g["T_sk_ref"].view(np.uint32))
+
+
+def test_against_cpu_oracle():
+    R = make_logits("normal", 1 << 14, seed=21)
+    G = make_logits("normal", 1 << 14, seed=22)
+    T = capi.birkhoff_proj_n4_tensor(R)
+    To = oracle.birkhoff_proj_n4(R.cpu().numpy(), 1e-6)
+    assert np.max(np.abs(T.cpu().numpy() - To)) < TOL
+    D = capi.birkhoff_proj_n4_backward_tensor(G, T)
+    Do = oracle.birkhoff_proj_n4_backward(G.cpu().numpy(), T.cpu().numpy())
+    assert np.max(np.abs(D.cpu().numpy() - Do)) < TOL
+
+
+def test_doubly_stochastic_at_workload_size():
+    """Rows sum to one and columns within 1e-5 on the N(0,1) workload."""
+    R = make_logits("normal", 1 << 22, seed=0)
+    T = capi.birkhoff_proj_n4_tensor(R).double()
+    assert (T.sum(2) - 1).abs().max().item() < TOL
+    assert (T.sum(1) - 1).abs().max().item() < TOL
+    assert T.min().item() >= 0
+
+
+# ---- Sinkhorn-Knopp pair -------------------------------------------------
+
+@pytest.mark.parametrize("kind", ["normal", "sigma_mix", "wide"])
+@pytest.mark.parametrize("iters", [0, 1, 7, 20, 35])
+def test_sinkhorn_forward_bitwise(ref, kind, iters):
+    M = torch.exp(make_logits(kind, 1 << 16, seed=iters))
+    T = capi.sinkhorn_knopp_n4_tensor(M, iters)
+    Tr = torch.empty_like(M)
+    ref.sinkhorn_knopp_n4(M.data_ptr(), Tr.data_ptr(), M.shape[0], iters, stream())
+    assert bitwise_equal(T, Tr)
+
+
+def test_sinkhorn_pair_matches_vanilla_autograd():
+    """The Sinkhorn-Knopp kernel configuration: N = 2^22, x ~ N(0,1), 20
+    iterations; forward and dR within 1e-5 of the vanilla PyTorch SK20."""
+    n = 1 << 22
+    x = make_logits("normal", n, seed=123)
+    G = make_logits("normal", n, seed=124)
+    M = torch.exp(x)
+    T = capi.sinkhorn_knopp_n4_tensor(M, 20)
+    dR = capi.sinkhorn_knopp_n4_backward_tensor(G, M, 20) * M
+    P, dRv = oracle.vanilla_sinkhorn(x, G)
+    assert (T - P).abs().max().item() < TOL
+    assert (dR - dRv).abs().max().item() < TOL
+
+
+@pytest.mark.parametrize("iters", [1, 2, 3, 4, 5, 9, 16, 19, 20])
+def test_sinkhorn_backward_every_iteration_count(iters):
+    n = 4096
+    M = torch.exp(make_logits("normal", n, seed=iters))
+    G = make_logits("normal", n, seed=iters + 50)
+    D = capi.sinkhorn_knopp_n4_backward_tensor(G, M, iters)
+    Do = oracle.sinkhorn_knopp_n4_backward(G.cpu().numpy(), M.cpu().numpy(), iters, 1e-8, exact=True)
+    assert np.max(np.abs(D.cpu().numpy() - Do)) < 2e-6
+    x = torch.log(M)
+    _, dRv = oracle.vanilla_sinkhorn(x, G, iters=iters)
+    assert (D * M - dRv).abs().max().item() < TOL
+
+
+def test_sinkhorn_backward_zero_iterations_is_identity():
+    M = torch.exp(make_logits("normal", 1000, seed=1))
+    G = make_logits("normal", 1000, seed=2)
+    assert torch.equal(capi.sinkhorn_knopp_n4_backward_tensor(G, M, 0), G)
