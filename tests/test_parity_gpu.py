@@ -135,12 +135,20 @@ def test_against_cpu_oracle():
     assert np.max(np.abs(D.cpu().numpy() - Do)) < TOL
 
 
-def test_doubly_stochastic_at_workload_size():
-    """Rows sum to one and columns within 1e-5 on the N(0,1) workload."""
+def test_doubly_stochastic_at_workload_size(ref):
+    """Rows sum to one (by construction, to rounding) and columns to within
+    1e-5 wherever the reference's Newton converges.  A few matrices in a
+    million stop at the 20-iteration cap with a column sum a little past
+    1e-5; the reference returns the same bits for them."""
     R = make_logits("normal", 1 << 22, seed=0)
-    T = capi.birkhoff_proj_n4_tensor(R).double()
-    assert (T.sum(2) - 1).abs().max().item() < TOL
-    assert (T.sum(1) - 1).abs().max().item() < TOL
+    T = capi.birkhoff_proj_n4_tensor(R)
+    Tr = ref_forward(ref, R)
+    assert bitwise_equal(T, Tr)
+    T = T.double()
+    assert (T.sum(2) - 1).abs().max().item() < 1e-6
+    col = (T.sum(1) - 1).abs().amax(1)
+    assert (col > TOL).float().mean().item() < 1e-5
+    assert col.max().item() < 1e-4
     assert T.min().item() >= 0
 
 
