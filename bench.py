@@ -48,7 +48,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=1 << 24, help="matrices per GPU")
+    ap.add_argument("--workload", choices=["newton", "sinkhorn"], default="newton",
+                    help="newton: the Newton forward + IFT backward (default, the headline metric); "
+                         "sinkhorn: the fused exp + Sinkhorn-Knopp pair, 20 iterations")
+    ap.add_argument("--n", type=int, default=None, help="matrices per GPU (default 2^24, or 2^22 for sinkhorn)")
     ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
     ap.add_argument("--tol", type=float, default=1e-6)
     ap.add_argument("--e2e-steps", type=int, default=3)
@@ -73,22 +76,33 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic_per_matrix():
-    """DRAM bytes per matrix of the forward kernel from the committed ncu
-    summary (profiles/roofline_traffic.json), or None."""
+def ncu_forward_counts():
+    """Per-matrix DRAM bytes, warp instructions and MUFU operations of the
+    forward kernel from the committed ncu summary
+    (profiles/roofline_traffic.json), or Nones."""
     p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
     try:
         with open(p) as f:
-            d = json.load(f)
-        return float(d["forward"]["dram_bytes_per_matrix"])
+            d = json.load(f)["forward"]
+        return (float(d["dram_bytes_per_matrix"]), float(d.get("warp_instructions_per_matrix", "nan")),
+                float(d.get("mufu_thread_ops_per_matrix", "nan")))
     except Exception:
-        return None
+        return None, None, None
+
+
+def sm_count(dev):
+    import torch
+
+    return torch.cuda.get_device_properties(dev).multi_processor_count
 
 
 def workload_config(args, world):
+    if args.workload == "sinkhorn":
+        what = "fused exp + Sinkhorn-Knopp n4 (20 iterations) forward + backward"
+    else:
+        what = f"Newton forward (tol {args.tol:g}) + IFT backward"
     return {
-        "workload": f"Newton forward (tol {args.tol:g}) + IFT backward, N=2^{args.n.bit_length() - 1} fp32 4x4 "
-                    f"per GPU, x~{args.dist}, G~N(0,1)",
+        "workload": f"{what}, N=2^{args.n.bit_length() - 1} fp32 4x4 per GPU, x~{args.dist}, G~N(0,1)",
         "n_per_gpu": args.n,
         "global_batch": args.n * world,
         "tol": args.tol,
@@ -270,19 +284,23 @@ def run_ours(args):
     from mhc_proj.workloads import make_logits
 
     n = args.n
-    proj = mhc_proj.torch.birkhoff_proj_n4
-    proj_bwd = mhc_proj.torch.birkhoff_proj_n4_backward
     R = make_logits(args.dist, n, seed=1000 + rank, device=dev)
     G = make_logits("normal", n, seed=2000 + rank, device=dev)
     tol = args.tol
+    if args.workload == "sinkhorn":
+        fwd = lambda: mhc_proj.torch.sinkhorn_knopp_n4_logits(R, 20)["T"]  # noqa: E731
+        bwd = lambda T: mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(G, R, 20)["D"]  # noqa: E731
+    else:
+        fwd = lambda: mhc_proj.torch.birkhoff_proj_n4(R, tol)["T"]  # noqa: E731
+        bwd = lambda T: mhc_proj.torch.birkhoff_proj_n4_backward(G, T)["D"]  # noqa: E731
 
     def step(ev=None):
         if ev is not None:
             ev[0].record()
-        T = proj(R, tol)["T"]
+        T = fwd()
         if ev is not None:
             ev[1].record()
-        D = proj_bwd(G, T)["D"]
+        D = bwd(T)
         if ev is not None:
             ev[2].record()
         return T, D
@@ -312,7 +330,8 @@ def run_ours(args):
 
     # end to end through the public API with host buffers: pinned inputs go
     # up, T and D come back, chunks pipelined over two streams
-    e2e = run_e2e(args, R, G, dev, world)
+    e2e = run_e2e(args, R, G, dev, world) if args.workload == "newton" else {"ms": float("nan"), "h2d": 0, "d2h": 0, "how": "not measured for this workload"}
+    unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
 
     stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
     if world > 1:
@@ -325,7 +344,21 @@ def run_ours(args):
         fwd_gbs = BYTES_FWD * n / (fwd_ms * 1e-3) / 1e9
         bwd_gbs = BYTES_BWD * n / (bwd_ms * 1e-3) / 1e9
         step_gbs = (BYTES_FWD + BYTES_BWD) * n / (ms_per_step * 1e-3) / 1e9
-        tpm = ncu_traffic_per_matrix()
+        tpm, wipm, mufupm = ncu_forward_counts()
+        sms = sm_count(dev)
+        clocks = clk.summary()
+        mhz = clocks["sm_mhz"] if clocks else 1965.0
+        rate_fwd = n / (fwd_ms * 1e-3)  # matrices/s through the forward kernel
+        compute = None
+        if wipm == wipm and mufupm == mufupm:  # not NaN
+            issue_peak = sms * 4 * mhz * 1e6          # warp instructions/s: one per SM sub-partition per clock
+            mufu_peak = sms * 16 * mhz * 1e6          # MUFU results/s: 16 per SM per clock
+            compute = {"bound": "issue", "unit": "warp instructions/s",
+                       "achieved": rate_fwd * wipm, "peak": issue_peak, "frac": rate_fwd * wipm / issue_peak,
+                       "mufu_frac": rate_fwd * mufupm / mufu_peak,
+                       "per_matrix": {"warp_instructions": wipm, "mufu_ops": mufupm},
+                       "source": "per-matrix counts from ncu (profiles/roofline_traffic.json) x live forward rate; "
+                                 "peaks from the SM count and the median SM clock seen"}
         line = {
             "metric": METRIC,
             "value": world * n / (ms_per_step * 1e-3),
@@ -341,7 +374,9 @@ def run_ours(args):
             "data": "synthetic (seeded torch generators; workload shape and distribution)",
             "config": workload_config(args, world),
             "roofline": {
-                "bound": "hbm", "kernel": "birkhoff_fwd_kernel (Newton forward)",
+                "bound": "hbm",
+                "kernel": "sk_fwd_kernel (fused exp + Sinkhorn-Knopp)" if args.workload == "sinkhorn"
+                          else "birkhoff_fwd_kernel (Newton forward)",
                 "achieved": fwd_gbs, "peak": peak, "unit": "GB/s", "frac": fwd_gbs / peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "algorithmic_bytes_per_matrix": BYTES_FWD,
@@ -351,14 +386,24 @@ def run_ours(args):
                 "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms,
                             "forward_gbs": fwd_gbs, "backward_gbs": bwd_gbs,
                             "backward_frac": bwd_gbs / peak},
+                "compute": compute,
             },
             "e2e": {"value": world * n / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "ms_per_step": e2e_ms, "how": e2e["how"]},
             "gpu_launches": 2 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if args.workload == "sinkhorn":
+            line["metric"] = "Sinkhorn-Knopp n4 (20 iterations) fwd+bwd matrices/s"
+            line["roofline"]["compute"] = None
+            line["roofline"]["traffic"] = None
+            line["e2e"] = None
+            line["unfused_reference_composition"] = {
+                "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
+                "how": "torch.exp, sinkhorn_knopp_n4, sinkhorn_knopp_n4_backward, product with exp(R) "
+                       "(the reference MHCSinkhornN4 composition) on this repository's kernels"}
+        if world == 1 and not args.no_cpu_baseline and args.workload == "newton":
             rate, nt, done = cpu_port_rate(args.cpu_seconds, 1 << 18, args.dist, tol)
             line["cpu_baseline"] = {
                 "value": rate, "unit": UNIT, "cores": nt, "kind": "port",
@@ -373,28 +418,53 @@ def run_ours(args):
     return 0
 
 
+def sinkhorn_unfused_ms(R, G, steps):
+    """Device time of the reference's MHCSinkhornN4 composition (module.py:46-72)
+    on this repository's unfused kernels: exp, SK forward, SK backward, product."""
+    import torch
+
+    import mhc_proj
+
+    def once():
+        M = torch.exp(R)
+        mhc_proj.torch.sinkhorn_knopp_n4(M, 20)
+        return mhc_proj.torch.sinkhorn_knopp_n4_backward(G, M, 20)["D"] * M
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
 def run_e2e(args, R, G, dev, world):
     """End to end through mhc_proj.torch.* with host buffers: each step copies
     R and G from pinned host memory, runs the forward and backward, and copies
-    T and D back to pinned host memory; the batch moves in chunks over two
+    T and D back to pinned host memory; the batch moves in chunks over three
     streams so copies in both directions overlap the kernels."""
     import torch
 
     import mhc_proj
 
     n = R.shape[0]
-    chunks = 8 if n >= (1 << 20) else 1
+    chunks = 16 if n >= (1 << 20) else 1
     Rh = R.cpu().pin_memory()
     Gh = G.cpu().pin_memory()
     Th = torch.empty_like(Rh).pin_memory()
     Dh = torch.empty_like(Rh).pin_memory()
-    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
     bounds = [(n * i // chunks, n * (i + 1) // chunks) for i in range(chunks)]
     tol = args.tol
 
     def step():
         for i, (a, b) in enumerate(bounds):
-            s = streams[i % 2]
+            s = streams[i % len(streams)]
             with torch.cuda.stream(s):
                 r = Rh[a:b].to(dev, non_blocking=True)
                 g = Gh[a:b].to(dev, non_blocking=True)
@@ -425,11 +495,13 @@ def run_e2e(args, R, G, dev, world):
     nbytes = n * 64
     return {"ms": ms, "h2d": 2 * nbytes, "d2h": 2 * nbytes,
             "how": f"pinned host R,G -> device -> fwd+bwd (public API) -> T,D to pinned host; "
-                   f"{chunks} chunks over 2 streams; {args.e2e_steps} steps timed with CUDA events"}
+                   f"{chunks} chunks over {len(streams)} streams; {args.e2e_steps} steps timed with CUDA events"}
 
 
 def main():
     args = parse_args()
+    if args.n is None:
+        args.n = (1 << 22) if args.workload == "sinkhorn" else (1 << 24)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

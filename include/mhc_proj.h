@@ -66,13 +66,32 @@ MHC_API int mhc_sinkhorn_knopp_n4(const float* d_M, float* d_T, int64_t N, int n
                           cudaStream_t stream);
 
 /* Exact gradient of sum(G .* sinkhorn_knopp_n4(M)) with respect to M.
- * num_iters <= 0 copies G to D; num_iters > MHC_SK_BACKWARD_MAX_ITERS
+ * num_iters <= 0 gives D = G; num_iters > MHC_SK_BACKWARD_MAX_ITERS
  * returns MHC_ERR_ITERS.
  * Replaces: void sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M,
  *           float* d_D, int N, int num_iters, cudaStream_t)
  *           -- src/sinkhorn_knopp_n4.cu:13 */
 MHC_API int mhc_sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M, float* d_D,
                                    int64_t N, int num_iters, cudaStream_t stream);
+
+/* Sinkhorn-Knopp fused with the exponential: the input is the logits R and
+ * the kernel forms M = exp(R) (the accurate expf, as torch.exp computes it)
+ * before the normalisations above.  Same result as mhc_sinkhorn_knopp_n4 on
+ * M = torch.exp(R), in one pass over HBM (128 B per matrix instead of 256).
+ * No reference counterpart: it fuses the torch.exp that the reference's
+ * MHCSinkhornN4Function does in Python (mhc_proj/module.py:50) into the
+ * kernel. */
+MHC_API int mhc_sinkhorn_knopp_n4_logits(const float* d_R, float* d_T, int64_t N, int num_iters,
+                                         cudaStream_t stream);
+
+/* Gradient with respect to R of sum(G .* sinkhorn_knopp_n4(exp(R))): the
+ * backward above times exp(R), in one pass (192 B per matrix instead of
+ * 384).  No reference counterpart: it fuses the backward kernel with the
+ * D * expon product of the reference's MHCSinkhornN4Function.backward
+ * (mhc_proj/module.py:70).  num_iters > MHC_SK_BACKWARD_MAX_ITERS returns
+ * MHC_ERR_ITERS. */
+MHC_API int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const float* d_R, float* d_D,
+                                                  int64_t N, int num_iters, cudaStream_t stream);
 
 /* Human-readable text for a return code of the functions above. */
 MHC_API const char* mhc_status_string(int status);

@@ -30,14 +30,20 @@ CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 CXX = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
 
-CU_SOURCES = ["birkhoff_n4.cu", "sinkhorn_n4.cu"]
-# --use_fast_math matches the reference's build (setup.py:28): the kernels
-# reproduce its fast exp/log/divide results exactly.
-NVCC_FLAGS = [
-    "-O3", "--use_fast_math", "-std=c++17", "-lineinfo",
+COMMON_FLAGS = [
+    "-O3", "-std=c++17", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
 ]
+# Per-source math flags.  The Newton kernels take --use_fast_math, as the
+# reference's build does (setup.py:28), so their exp/log/divide give its
+# results exactly.  The Sinkhorn-Knopp kernels use only explicitly rounded
+# operations and a correctly rounded reciprocal; they keep the reference's
+# flush-to-zero but take the accurate expf for the fused exp(R) kernels.
+CU_SOURCES = {
+    "birkhoff_n4.cu": ["--use_fast_math"],
+    "sinkhorn_n4.cu": ["-ftz=true", "-prec-div=true", "-prec-sqrt=true", "-fmad=true"],
+}
 
 LIB = os.path.join(PKG, "libmhcproj.so")
 EXT = os.path.join(PKG, "_internal" + sysconfig.get_config_var("EXT_SUFFIX"))
@@ -64,11 +70,11 @@ def _headers() -> list[str]:
 def build_cuda_lib(force: bool = False, verbose: bool = True) -> str:
     os.makedirs(BUILD, exist_ok=True)
     objs = []
-    for src in CU_SOURCES:
+    for src, math_flags in CU_SOURCES.items():
         s = os.path.join(CSRC, src)
         o = os.path.join(BUILD, src.replace(".cu", ".o"))
         if force or _stale(o, [s, *_headers(), __file__]):
-            _run([NVCC, *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o], verbose)
+            _run([NVCC, *COMMON_FLAGS, *math_flags, "-I", INCLUDE, "-I", CSRC, "-c", s, "-o", o], verbose)
         objs.append(o)
     if force or _stale(LIB, objs):
         _run([NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", LIB,

@@ -24,19 +24,26 @@ enum Stage : int {
 // for one matrix as a state machine, and a lane that finishes stores its T and
 // takes the warp's next matrix, so a warp costs the sum of its matrices' work
 // over 32 instead of the maximum over each group of 32 (per-matrix work ranges
-// from 4 to ~130 evaluations).
+// from 4 to ~140 evaluations).
 //
 // Every step is the same straight-line code for every lane: the Newton
 // direction at the lane's current point, one log-sum-exp pass whose lines are
 // rows or columns as the stage needs, the row and the column
 // post-processing, and the transition, all as selects.  No branch depends on
 // a lane's stage, so lanes at different points of the algorithm never split
-// the warp; the only branch is the warp-wide refill.
+// the warp; the only branches are the warp-wide refill and the stores.
+//
+// The current point keeps only what the next direction needs -- the column
+// sums, the six Gram sums of T, f and |g| -- not T itself: T is written to
+// the output by the pass that finishes the matrix.  The beta = 0 evaluation
+// writes its T as well, for the one exit that comes after a column pass (the
+// alpha = 0 initialisation rejected and beta = 0 already converged).
 template <class Rd, bool kVec>
 __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float* __restrict__ R,
                                                                     float* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_warp)
 {
+    using Prod = typename Rd::P;
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t begin = warp * per_warp;
@@ -44,8 +51,8 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
     if (begin >= end) return;  // warp-uniform
 
     Mat4 r;                 // logits of the lane's matrix
-    Mat4 T;                 // T at the current point
-    float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // column sums of T
+    float p[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // Gram sums of T at the current point
+    float c[3] = {0.0f, 0.0f, 0.0f};  // column sums of T (the fourth is never used)
     float f = 0.0f;         // objective at the current point
     float gn = 0.0f;        // gradient l1 norm at the current point
     float alpha[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row LSE at the current point
@@ -55,8 +62,6 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
     bool fresh = false;     // a new Newton iteration starts: take the direction now
     int64_t idx = begin + lane;
     int stage = kIdle;
-#pragma unroll
-    for (int e2 = 0; e2 < 16; ++e2) T.m[e2] = 0.0f;
     if (idx < end) {
         load_mat<kVec>(R, idx, r);
         stage = kEval0;
@@ -67,40 +72,42 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
     int64_t next = min(end, begin + 32);
 
     while (__any_sync(kFullMask, stage != kIdle)) {
+        const bool s_eval0 = stage == kEval0, s_alpha0 = stage == kAlpha0, s_evala = stage == kEvalA;
+        const bool s_cand = stage == kCand, s_skcol = stage == kSkCol, s_skeval = stage == kSkEval;
+
         // Direction at the current point; kept only by lanes starting a new
         // Newton iteration (compute_newton_direction, :443-445).
         {
             float dn[4];
-            newton_direction<Rd>(T, c, gn, dn);
+            newton_direction<Rd>(p, c, gn, dn);
 #pragma unroll
             for (int j = 0; j < 4; ++j) d[j] = fresh ? dn[j] : d[j];
             k = fresh ? 0 : k;
             fresh = false;
         }
-        const bool col = stage == kAlpha0 || stage == kSkCol;
+        const bool col = s_alpha0 || s_skcol;
         const float gamma = line_step(k);
-        float v[4];  // point of evaluation (rows) or row offsets (columns)
+        // Point of evaluation (rows) or per-row offsets (columns).  -0 is the
+        // offset of the alpha = 0 pass: x + (-0) == x for every x, so that pass
+        // sees R itself, as in the reference.
+        float v[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+            const float base = s_skcol ? alpha[j] : beta[j];
             const float cand = __fmaf_rn(gamma, d[j], beta[j]);
-            v[j] = stage == kEval0 ? 0.0f : stage == kCand ? cand : stage == kSkCol ? alpha[j] : beta[j];
+            const float vj = s_cand ? cand : base;
+            v[j] = s_eval0 ? 0.0f : s_alpha0 ? -0.0f : vj;
         }
-        // Line-major input: rows of v + R, columns of R offset by v per row,
-        // or raw columns of R for the alpha = 0 initialisation.
         float X[16];
 #pragma unroll
         for (int l = 0; l < 4; ++l)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const float rv = col ? r.m[4 * q + l] : r.m[4 * l + q];
-                const float sum = v[q] + rv;
-                X[4 * l + q] = stage == kAlpha0 ? rv : sum;
-            }
+            for (int q = 0; q < 4; ++q) X[4 * l + q] = v[q] + (col ? r.m[4 * q + l] : r.m[4 * l + q]);
         float e[16], s[4], lse[4];
         lse_pass(X, e, s, lse);
 
         // Row post-processing: T, column sums, f and |g| at v
-        // (compute_f_gradient, :235-254).
+        // (compute_f_gradient, :235-254), and the Gram sums of T.
         Mat4 Tn;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -108,25 +115,28 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
 #pragma unroll
             for (int j = 0; j < 4; ++j) Tn.m[4 * i + j] = __fmul_rn(e[4 * i + j], rs);
         }
-        float cn[4];
+        float cn[3];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) cn[j] = psum4(Tn.m[j], Tn.m[4 + j], Tn.m[8 + j], Tn.m[12 + j]);
+        for (int j = 0; j < 3; ++j) cn[j] = psum4(Tn.m[j], Tn.m[4 + j], Tn.m[8 + j], Tn.m[12 + j]);
         const float fn = -psum4(lse[0], lse[1], lse[2], lse[3]) - psum4(v[0], v[1], v[2], v[3]);
         const float gnn = __fadd_rn(__fadd_rn(fabsf(cn[0] - 1.0f), fabsf(cn[1] - 1.0f)), fabsf(cn[2] - 1.0f));
-        // Column post-processing: b = column LSE, beta' = b - b_3, and the
-        // objective at alpha = 0 (:139-146, :168-174).
+        float pn[6];
+        gram_sums<Prod>(Tn.m, pn);
+        // Column post-processing: the objective at alpha = 0 (:143); the new
+        // beta = b - b_3 is formed below (:139-146, :168-174).
         const float fa = -psum4(lse[0], lse[1], lse[2], lse[3]);
 
         // Transition.
-        const bool accept = stage == kCand && fn < f && gnn < gn;
-        const bool adopt = stage == kEval0 || stage == kEvalA || stage == kSkEval || accept;
-        const bool take_a0 = stage == kAlpha0 && fa < f;
-        const bool newbeta = take_a0 || stage == kSkCol;
+        const bool accept = s_cand && fn < f && gnn < gn;
+        const bool adopt = s_eval0 || s_evala || s_skeval || accept;
+        const bool take_a0 = s_alpha0 && fa < f;
+        const bool newbeta = take_a0 || s_skcol;
 #pragma unroll
-        for (int e2 = 0; e2 < 16; ++e2) T.m[e2] = adopt ? Tn.m[e2] : T.m[e2];
+        for (int q = 0; q < 6; ++q) p[q] = adopt ? pn[q] : p[q];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) c[j] = adopt ? cn[j] : c[j];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            c[j] = adopt ? cn[j] : c[j];
             alpha[j] = adopt ? lse[j] : alpha[j];
             const float bj = lse[j] - lse[3];
             beta[j] = adopt ? v[j] : newbeta ? bj : beta[j];
@@ -135,30 +145,31 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
         gn = adopt ? gnn : gn;
         // the first convergence test after initialisation (:426-431), or the
         // test at the end of a Newton iteration (:490-494)
-        const bool check_init = stage == kEvalA || (stage == kAlpha0 && !take_a0);
-        const bool end_iter = accept || stage == kSkEval;
+        const bool check_init = s_evala || (s_alpha0 && !take_a0);
+        const bool end_iter = accept || s_skeval;
         const int it_next = check_init ? 0 : end_iter ? it + 1 : it;
         const bool converged = (check_init || end_iter) && gn < tol;
         const bool done = converged || (end_iter && it_next == kNewtonMaxIters);
         const bool next_iter = (check_init || end_iter) && !done;
         it = it_next;
-        const bool reject_last = stage == kCand && !accept && k == kLineSearchMaxIters - 1;
-        k = (stage == kCand && !accept) ? k + 1 : k;
+        const bool reject_last = s_cand && !accept && k == kLineSearchMaxIters - 1;
+        k = (s_cand && !accept) ? k + 1 : k;
         fresh = next_iter;
         stage = stage == kIdle ? kIdle
               : done           ? kIdle
               : next_iter      ? kCand
-              : stage == kEval0 ? kAlpha0
+              : s_eval0        ? kAlpha0
               : take_a0        ? kEvalA
               : reject_last    ? kSkCol
-              : stage == kSkCol ? kSkEval
+              : s_skcol        ? kSkEval
                                : stage;
 
-        // Retire finished matrices and hand their lanes the warp's next ones.
+        // T leaves with the pass that produced it.
+        if (s_eval0 || (done && !col)) store_mat<kVec>(Tout, idx, Tn);
+        // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);
         if (want) {
             if (done) {
-                store_mat<kVec>(Tout, idx, T);
                 idx = next + __popc(want & ((1u << lane) - 1u));
                 if (idx < end) {
                     load_mat<kVec>(R, idx, r);

@@ -206,25 +206,41 @@ __device__ __forceinline__ void lse_pass(const float X[16], float e[16], float s
     }
 }
 
-// Leading 3x3 block of diag(c) - T^T T plus `shift` on the diagonal, as the
-// row-0 lanes of the reference hold it (they broadcast H,
-// birkhoff_proj_n4.cu:286-309 and :550-573).  The off-diagonal pairs are
-// (0,1), (1,2), (2,0), the column rotation the reference uses.
+// Column products of T summed over rows, as the row-0 lanes of the reference
+// hold them (they broadcast H, birkhoff_proj_n4.cu:286-309 and :550-573):
+// p[0..2] = sum_i T_ij^2 for j = 0,1,2 and p[3..5] = sum_i T_ij T_ik for the
+// column pairs (0,1), (1,2), (2,0), the rotation the reference uses.
 template <class Prod>
-__device__ __forceinline__ Sym3 gram3(const Mat4& T, const float c[4], float shift)
+__device__ __forceinline__ void gram_sums(const float* t, float p[6])
 {
-    const float* t = T.m;
+    p[0] = Prod::prod_sum(0, t[0], t[0], t[4], t[4], t[8], t[8], t[12], t[12]);
+    p[1] = Prod::prod_sum(0, t[1], t[1], t[5], t[5], t[9], t[9], t[13], t[13]);
+    p[2] = Prod::prod_sum(0, t[2], t[2], t[6], t[6], t[10], t[10], t[14], t[14]);
+    p[3] = Prod::prod_sum(0, t[0], t[1], t[4], t[5], t[8], t[9], t[12], t[13]);
+    p[4] = Prod::prod_sum(0, t[1], t[2], t[5], t[6], t[9], t[10], t[13], t[14]);
+    p[5] = Prod::prod_sum(0, t[2], t[0], t[6], t[4], t[10], t[8], t[14], t[12]);
+}
+
+// Leading 3x3 block of diag(c) - T^T T plus `shift` on the diagonal, from
+// the sums above.
+__device__ __forceinline__ Sym3 gram_matrix(const float p[6], const float c[3], float shift)
+{
     Sym3 h;
-    const float p0 = Prod::prod_sum(0, t[0], t[0], t[4], t[4], t[8], t[8], t[12], t[12]);
-    const float p1 = Prod::prod_sum(0, t[1], t[1], t[5], t[5], t[9], t[9], t[13], t[13]);
-    const float p2 = Prod::prod_sum(0, t[2], t[2], t[6], t[6], t[10], t[10], t[14], t[14]);
-    h.h00 = __fsub_rn(__fadd_rn(shift, c[0]), p0);
-    h.h11 = __fsub_rn(__fadd_rn(shift, c[1]), p1);
-    h.h22 = __fsub_rn(__fadd_rn(shift, c[2]), p2);
-    h.h01 = -Prod::prod_sum(0, t[0], t[1], t[4], t[5], t[8], t[9], t[12], t[13]);
-    h.h12 = -Prod::prod_sum(0, t[1], t[2], t[5], t[6], t[9], t[10], t[13], t[14]);
-    h.h02 = -Prod::prod_sum(0, t[2], t[0], t[6], t[4], t[10], t[8], t[14], t[12]);
+    h.h00 = __fsub_rn(__fadd_rn(shift, c[0]), p[0]);
+    h.h11 = __fsub_rn(__fadd_rn(shift, c[1]), p[1]);
+    h.h22 = __fsub_rn(__fadd_rn(shift, c[2]), p[2]);
+    h.h01 = -p[3];
+    h.h12 = -p[4];
+    h.h02 = -p[5];
     return h;
+}
+
+template <class Prod>
+__device__ __forceinline__ Sym3 gram3(const Mat4& T, const float c[3], float shift)
+{
+    float p[6];
+    gram_sums<Prod>(T.m, p);
+    return gram_matrix(p, c, shift);
 }
 
 // Newton direction d = -H^{-1} g with H = diag(c) - T^T T + min(|g|^2, 1e-3) I,
@@ -232,10 +248,10 @@ __device__ __forceinline__ Sym3 gram3(const Mat4& T, const float c[4], float shi
 // (compute_newton_direction, :263-367).  d[3] is the reference's fourth-lane
 // value: +0 on the gradient fallback, -0 * (1/det) on the Newton branch.
 template <class Rd>
-__device__ __forceinline__ void newton_direction(const Mat4& T, const float c[4], float gnorm, float d[4])
+__device__ __forceinline__ void newton_direction(const float p[6], const float c[3], float gnorm, float d[4])
 {
     const float shift = fminf(gnorm * gnorm, 1e-3f);
-    const Sym3 h = gram3<typename Rd::P>(T, c, shift);
+    const Sym3 h = gram_matrix(p, c, shift);
     const float g0 = c[0] - 1.0f;
     const float g1 = c[1] - 1.0f;
     const float g2 = c[2] - 1.0f;

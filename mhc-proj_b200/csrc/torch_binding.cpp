@@ -11,6 +11,9 @@
 //     dtype/device; the backward converts T to G's dtype/device;
 //   - sinkhorn_knopp_n4_backward with max_iter > 20 raises ValueError;
 //   - extra keyword arguments are accepted and ignored.
+// Two functions have no reference counterpart: sinkhorn_knopp_n4_logits and
+// its backward take the logits R and fuse exp(R) (and, backward, the product
+// with exp(R)) into the kernels.
 // Differences: kernels run on PyTorch's current stream of the target device
 // (the reference uses cudaStreamPerThread), batch sizes are 64-bit, B = 0 is
 // a no-op, and a failed launch raises RuntimeError.
@@ -132,6 +135,50 @@ py::dict sinkhorn_knopp_n4_backward(torch::Tensor G, torch::Tensor M, int max_it
     return out;
 }
 
+// Fused exp + Sinkhorn-Knopp on the logits R (no reference counterpart: the
+// reference forms exp(R) in Python, mhc_proj/module.py:50,70).
+py::dict sinkhorn_knopp_n4_logits(torch::Tensor R, int max_iter, const py::kwargs&)
+{
+    check_batch(R, "R");
+    const auto src = R.options();
+    const auto opts = target_options(R);
+    R = R.to(opts);
+    const c10::cuda::CUDAGuard guard(R.device());
+    R = R.contiguous();
+    const int64_t n = R.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_sinkhorn_knopp_n4_logits(R.data_ptr<float>(), T.data_ptr<float>(), n, max_iter,
+                                              current_stream()),
+                 "sinkhorn_knopp_n4_logits");
+    py::dict out;
+    out["T"] = T.to(src);
+    return out;
+}
+
+py::dict sinkhorn_knopp_n4_logits_backward(torch::Tensor G, torch::Tensor R, int max_iter, const py::kwargs&)
+{
+    check_batch(G, "G");
+    check_batch(R, "R", G.size(0));
+    if (max_iter > MHC_SK_BACKWARD_MAX_ITERS)
+        throw std::invalid_argument("sinkhorn_knopp_n4_logits_backward supports max_iter <= " +
+                                    std::to_string(MHC_SK_BACKWARD_MAX_ITERS));
+    const auto src = G.options();
+    const auto opts = target_options(G);
+    G = G.to(opts);
+    R = R.to(opts);
+    const c10::cuda::CUDAGuard guard(G.device());
+    G = G.contiguous();
+    R = R.contiguous();
+    const int64_t n = G.size(0);
+    torch::Tensor D = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_sinkhorn_knopp_n4_logits_backward(G.data_ptr<float>(), R.data_ptr<float>(),
+                                                       D.data_ptr<float>(), n, max_iter, current_stream()),
+                 "sinkhorn_knopp_n4_logits_backward");
+    py::dict out;
+    out["D"] = D.to(src);
+    return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_internal, m)
@@ -147,4 +194,9 @@ PYBIND11_MODULE(_internal, m)
                 "Sinkhorn-Knopp algorithm for 4x4 matrices");
     m_torch.def("sinkhorn_knopp_n4_backward", &sinkhorn_knopp_n4_backward, py::arg("G"), py::arg("M"),
                 py::arg("max_iter") = 20, "Sinkhorn-Knopp algorithm for 4x4 matrices, backward pass");
+    m_torch.def("sinkhorn_knopp_n4_logits", &sinkhorn_knopp_n4_logits, py::arg("R"), py::arg("max_iter") = 20,
+                "Sinkhorn-Knopp on exp(R) in one kernel (R: logits)");
+    m_torch.def("sinkhorn_knopp_n4_logits_backward", &sinkhorn_knopp_n4_logits_backward, py::arg("G"),
+                py::arg("R"), py::arg("max_iter") = 20,
+                "Gradient with respect to R of Sinkhorn-Knopp on exp(R), in one kernel");
 }

@@ -18,9 +18,12 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_backward",
     "mhc_sinkhorn_knopp_n4",
     "mhc_sinkhorn_knopp_n4_backward",
+    "mhc_sinkhorn_knopp_n4_logits",
+    "mhc_sinkhorn_knopp_n4_logits_backward",
     "mhc_status_string",
     "mhc_abi_version",
 )
+_LAUNCHERS = EXPORTED[:6]
 
 MHC_OK = 0
 MHC_ERR_INVALID_VALUE = -1
@@ -48,7 +51,9 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_backward.argtypes = [vp, vp, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_backward.argtypes = [vp, vp, vp, i64, i32, vp]
-        for f in EXPORTED[:4]:
+        L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
+        for f in _LAUNCHERS:
             getattr(L, f).restype = ctypes.c_int
         L.mhc_status_string.argtypes = [ctypes.c_int]
         L.mhc_status_string.restype = ctypes.c_char_p
@@ -85,6 +90,15 @@ def sinkhorn_knopp_n4(M: int, T: int, N: int, num_iters: int, stream: int = 0) -
 
 def sinkhorn_knopp_n4_backward(G: int, M: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:
     _check(lib().mhc_sinkhorn_knopp_n4_backward(G, M, D, N, num_iters, stream), "mhc_sinkhorn_knopp_n4_backward")
+
+
+def sinkhorn_knopp_n4_logits(R: int, T: int, N: int, num_iters: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_logits(R, T, N, num_iters, stream), "mhc_sinkhorn_knopp_n4_logits")
+
+
+def sinkhorn_knopp_n4_logits_backward(G: int, R: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_logits_backward(G, R, D, N, num_iters, stream),
+           "mhc_sinkhorn_knopp_n4_logits_backward")
 
 
 # --- tensor conveniences ---------------------------------------------------
@@ -133,4 +147,20 @@ def sinkhorn_knopp_n4_backward_tensor(G, M, num_iters: int = 20, out=None):
 
     D = torch.empty_like(G) if out is None else out
     sinkhorn_knopp_n4_backward(_dev(G, "G"), _dev(M, "M"), _dev(D, "D"), G.shape[0], num_iters, _stream(G))
+    return D
+
+
+def sinkhorn_knopp_n4_logits_tensor(R, num_iters: int = 20, out=None):
+    import torch
+
+    T = torch.empty_like(R) if out is None else out
+    sinkhorn_knopp_n4_logits(_dev(R, "R"), _dev(T, "T"), R.shape[0], num_iters, _stream(R))
+    return T
+
+
+def sinkhorn_knopp_n4_logits_backward_tensor(G, R, num_iters: int = 20, out=None):
+    import torch
+
+    D = torch.empty_like(G) if out is None else out
+    sinkhorn_knopp_n4_logits_backward(_dev(G, "G"), _dev(R, "R"), _dev(D, "D"), G.shape[0], num_iters, _stream(G))
     return D

@@ -5,8 +5,13 @@ mhc_proj/module.py:5-84:
   MHCProjectionN4(tol=1e-6)      forward: Newton projection, saves T;
                                  backward: implicit-function-theorem kernel.
   MHCSinkhornN4(max_iter=20)     forward: exp then fixed-iteration
-                                 Sinkhorn-Knopp, saves exp(R); backward: the
-                                 Sinkhorn-Knopp backward kernel times exp(R).
+                                 Sinkhorn-Knopp; backward: the Sinkhorn-Knopp
+                                 backward times exp(R).  For fp32 CUDA inputs
+                                 both run as one fused kernel each on the
+                                 logits (saving R, 320 instead of 640 bytes
+                                 of HBM traffic per matrix); other inputs take
+                                 the reference's composition (torch.exp in
+                                 the input dtype, kernel on exp(R), saves it).
 Both take any tensor whose last two dimensions are 4 x 4 (ValueError
 otherwise) and return a tensor of the input's shape.  A ``None`` incoming
 gradient (possible because gradient materialisation is off) yields ``None``.
@@ -54,10 +59,16 @@ class MHCSinkhornN4Function(torch.autograd.Function):
     @staticmethod
     def forward(ctx, R, max_iter=20):
         in_shape = R.shape
-        expon = torch.exp(R.reshape(-1, 4, 4))
-        T = _internal.torch.sinkhorn_knopp_n4(expon, max_iter)["T"]
+        R3 = R.reshape(-1, 4, 4)
         ctx.max_iter = max_iter
-        ctx.save_for_backward(expon)
+        ctx.fused = R3.is_cuda and R3.dtype == torch.float32
+        if ctx.fused:
+            T = _internal.torch.sinkhorn_knopp_n4_logits(R3, max_iter)["T"]
+            ctx.save_for_backward(R3)
+        else:
+            expon = torch.exp(R3)
+            T = _internal.torch.sinkhorn_knopp_n4(expon, max_iter)["T"]
+            ctx.save_for_backward(expon)
         ctx.set_materialize_grads(False)
         return T.view(in_shape)
 
@@ -67,8 +78,11 @@ class MHCSinkhornN4Function(torch.autograd.Function):
             return None, None
         in_shape = grad_output.shape
         G = grad_output.reshape(-1, 4, 4)
-        (expon,) = ctx.saved_tensors
-        D = _internal.torch.sinkhorn_knopp_n4_backward(G, expon, ctx.max_iter)["D"] * expon
+        (saved,) = ctx.saved_tensors
+        if ctx.fused:
+            D = _internal.torch.sinkhorn_knopp_n4_logits_backward(G, saved, ctx.max_iter)["D"]
+        else:
+            D = _internal.torch.sinkhorn_knopp_n4_backward(G, saved, ctx.max_iter)["D"] * saved
         return D.view(in_shape), None
 
 

@@ -11,7 +11,8 @@ from mhc_proj import sharding
 
 def test_public_names():
     assert hasattr(mhc_proj, "MHCProjectionN4") and hasattr(mhc_proj, "MHCSinkhornN4")
-    for f in ("birkhoff_proj_n4", "birkhoff_proj_n4_backward", "sinkhorn_knopp_n4", "sinkhorn_knopp_n4_backward"):
+    for f in ("birkhoff_proj_n4", "birkhoff_proj_n4_backward", "sinkhorn_knopp_n4", "sinkhorn_knopp_n4_backward",
+              "sinkhorn_knopp_n4_logits", "sinkhorn_knopp_n4_logits_backward"):
         assert callable(getattr(mhc_proj.torch, f))
 
 
@@ -52,6 +53,15 @@ def test_low_level_rejects_non_batch(shape):
         mhc_proj.torch.birkhoff_proj_n4_backward(ok, x)
     with pytest.raises(RuntimeError):
         mhc_proj.torch.sinkhorn_knopp_n4_backward(x, ok)
+
+
+def test_fused_logits_signatures():
+    doc = mhc_proj.torch.sinkhorn_knopp_n4_logits.__doc__
+    assert "R: torch.Tensor" in doc and "= 20" in doc
+    doc = mhc_proj.torch.sinkhorn_knopp_n4_logits_backward.__doc__
+    assert "G: torch.Tensor" in doc and "R: torch.Tensor" in doc
+    with pytest.raises(RuntimeError):
+        mhc_proj.torch.sinkhorn_knopp_n4_logits(torch.zeros(2, 4, 3))
 
 
 def test_backward_batch_mismatch():

@@ -126,3 +126,28 @@ def test_second_device_keeps_its_index():
     T = mhc_proj.torch.birkhoff_proj_n4(R)["T"]
     assert T.device == R.device
     assert torch.equal(T.cpu(), capi.birkhoff_proj_n4_tensor(R.to("cuda:0")).cpu())
+
+
+def test_sinkhorn_module_uses_fused_kernels_and_keeps_other_dtypes():
+    x = make_logits("normal", 4096, seed=13)
+    G = make_logits("normal", 4096, seed=14)
+    # fp32 CUDA: fused kernels, same bits as the reference's composition
+    xa = x.clone().requires_grad_(True)
+    T = mhc_proj.MHCSinkhornN4()(xa)
+    (T * G).sum().backward()
+    M = torch.exp(x)
+    assert torch.equal(T.detach(), mhc_proj.torch.sinkhorn_knopp_n4(M)["T"])
+    assert torch.equal(xa.grad, mhc_proj.torch.sinkhorn_knopp_n4_backward(G, M)["D"] * M)
+    # float64: the reference composition in the input dtype
+    xd = x.double().requires_grad_(True)
+    Td = mhc_proj.MHCSinkhornN4()(xd)
+    assert Td.dtype == torch.float64
+    (Td * G.double()).sum().backward()
+    assert xd.grad.dtype == torch.float64
+    assert (xd.grad.float() - xa.grad).abs().max().item() < 1e-5
+
+
+def test_fused_logits_backward_iteration_limit():
+    R = make_logits("normal", 8, seed=15)
+    with pytest.raises(ValueError):
+        mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(R, R, 21)

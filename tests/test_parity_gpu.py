@@ -195,3 +195,44 @@ def test_sinkhorn_backward_zero_iterations_is_identity():
     M = torch.exp(make_logits("normal", 1000, seed=1))
     G = make_logits("normal", 1000, seed=2)
     assert torch.equal(capi.sinkhorn_knopp_n4_backward_tensor(G, M, 0), G)
+
+
+# ---- fused exp + Sinkhorn-Knopp (logits input) -------------------------------
+
+@pytest.mark.parametrize("kind", ["normal", "sigma_mix", "uniform"])
+@pytest.mark.parametrize("iters", [0, 1, 5, 20])
+def test_fused_logits_equals_exp_then_kernel(kind, iters):
+    """sinkhorn_knopp_n4_logits(R) is bit for bit the kernel on torch.exp(R),
+    and its backward is bit for bit the M-gradient times torch.exp(R) (the
+    reference's MHCSinkhornN4 composition, module.py:50,70)."""
+    n = 1 << 16
+    R = make_logits(kind, n, seed=31 + iters)
+    G = make_logits("normal", n, seed=32 + iters)
+    M = torch.exp(R)
+    assert bitwise_equal(capi.sinkhorn_knopp_n4_logits_tensor(R, iters), capi.sinkhorn_knopp_n4_tensor(M, iters))
+    D_unfused = capi.sinkhorn_knopp_n4_backward_tensor(G, M, iters) * M
+    assert bitwise_equal(capi.sinkhorn_knopp_n4_logits_backward_tensor(G, R, iters), D_unfused)
+
+
+def test_fused_logits_wide_inputs_within_tolerance():
+    """With N(0,100) logits exp(R) has subnormal entries, which the kernels
+    flush like the reference; agreement is then to the last few ulps."""
+    n = 1 << 16
+    R = make_logits("wide", n, seed=40)
+    G = make_logits("normal", n, seed=41)
+    M = torch.exp(R)
+    assert (capi.sinkhorn_knopp_n4_logits_tensor(R, 20) - capi.sinkhorn_knopp_n4_tensor(M, 20)).abs().max().item() < 1e-6
+    D_unfused = capi.sinkhorn_knopp_n4_backward_tensor(G, M, 20) * M
+    D = capi.sinkhorn_knopp_n4_logits_backward_tensor(G, R, 20)
+    assert torch.allclose(D, D_unfused, rtol=1e-5, atol=1e-6)
+
+
+def test_fused_logits_matches_vanilla_autograd():
+    n = 1 << 20
+    x = make_logits("normal", n, seed=123)
+    G = make_logits("normal", n, seed=124)
+    T = capi.sinkhorn_knopp_n4_logits_tensor(x, 20)
+    dR = capi.sinkhorn_knopp_n4_logits_backward_tensor(G, x, 20)
+    P, dRv = oracle.vanilla_sinkhorn(x, G)
+    assert (T - P).abs().max().item() < TOL
+    assert (dR - dRv).abs().max().item() < TOL
