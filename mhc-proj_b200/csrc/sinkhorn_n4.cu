@@ -31,12 +31,13 @@ __global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(const float* __restric
 {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
-    Mat4 x;
-    load_mat<kVec>(M, idx, x);
-    if constexpr (kLogits) exp_inplace(x);
+    Mat4 x0;
+    load_mat<kVec>(M, idx, x0);
+    if constexpr (kLogits) exp_inplace(x0);
+    Pairs x = to_pairs(x0);
 #pragma unroll 1
-    for (int it = 0; it < iters; ++it) sk_iteration(x.m, kSkEps, nullptr, nullptr, nullptr);
-    store_mat<kVec>(T, idx, x);
+    for (int it = 0; it < iters; ++it) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
+    store_mat<kVec>(T, idx, from_pairs(x));
 }
 
 // Backward with a compile-time iteration count.  Segment starts are kept in
@@ -50,48 +51,52 @@ __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restric
                                                           float* __restrict__ D, int64_t N)
 {
     constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-    __shared__ float ckpt[kNumSeg > 0 ? kNumSeg : 1][16][kSkBlock];
+    __shared__ float2 ckpt[kNumSeg > 0 ? kNumSeg : 1][8][kSkBlock];
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
     const int tid = threadIdx.x;
 
-    Mat4 x;
-    load_mat<kVec>(M, idx, x);
-    if constexpr (kLogits) exp_inplace(x);
+    Mat4 x0;
+    load_mat<kVec>(M, idx, x0);
+    if constexpr (kLogits) exp_inplace(x0);
+    Pairs x = to_pairs(x0);
 #pragma unroll
     for (int s = 0; s < kNumSeg; ++s) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) ckpt[s][e][tid] = x.m[e];
+        for (int q = 0; q < 8; ++q) ckpt[s][q][tid] = x.p[q];
         if (s + 1 < kNumSeg) {
 #pragma unroll
-            for (int k = 0; k < kSkSeg; ++k) sk_iteration(x.m, kSkEps, nullptr, nullptr, nullptr);
+            for (int k = 0; k < kSkSeg; ++k) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
         }
     }
 
-    Mat4 dy;
-    load_mat<kVec>(G, idx, dy);
+    Mat4 g0;
+    load_mat<kVec>(G, idx, g0);
+    Pairs dy = to_pairs(g0);
 #pragma unroll
     for (int s = kNumSeg - 1; s >= 0; --s) {
         constexpr int kFull = kSkSeg;
         const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kFull;
-        float xr[kSkSeg][16], ri[kSkSeg][4], ci[kSkSeg][4];
+        Pairs xr[kSkSeg];
+        float ri[kSkSeg][4], ci[kSkSeg][4];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) x.m[e] = ckpt[s][e][tid];
+        for (int q = 0; q < 8; ++q) x.p[q] = ckpt[s][q][tid];
 #pragma unroll
         for (int k = 0; k < kSkSeg; ++k)
-            if (k < len) sk_iteration(x.m, kSkEps, xr[k], ri[k], ci[k]);
+            if (k < len) sk_iteration(x, kSkEps, &xr[k], ri[k], ci[k]);
 #pragma unroll
         for (int k = kSkSeg - 1; k >= 0; --k)
-            if (k < len) sk_iteration_vjp(dy.m, xr[k], ri[k], ci[k]);
+            if (k < len) sk_iteration_vjp(dy, xr[k], ri[k], ci[k]);
     }
     if constexpr (kLogits) {
         Mat4 m;
         load_mat<kVec>(M, idx, m);
         exp_inplace(m);
+        const Pairs mp = to_pairs(m);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) dy.m[e] = __fmul_rn(dy.m[e], m.m[e]);
+        for (int q = 0; q < 8; ++q) dy.p[q] = __fmul2_rn(dy.p[q], mp.p[q]);
     }
-    store_mat<kVec>(D, idx, dy);
+    store_mat<kVec>(D, idx, from_pairs(dy));
 }
 
 template <int kIters, bool kLogits>

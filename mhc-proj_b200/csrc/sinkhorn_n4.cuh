@@ -28,6 +28,36 @@ constexpr int kSkSeg = 4;
 
 __device__ __forceinline__ float sk_inv(float s, float eps) { return (s > eps) ? __frcp_rn(s) : 0.0f; }
 
+// A matrix as eight float2 pairs, two per row: P[2i] = (x_i0, x_i1),
+// P[2i+1] = (x_i2, x_i3).  Column-wise work then runs on packed fp32x2
+// arithmetic (two IEEE round-to-nearest operations per instruction on
+// sm_100), so column sums, column scaling and the column step of the
+// backward take half the instructions; row sums stay scalar, left to right.
+struct Pairs {
+    float2 p[8];
+};
+
+__device__ __forceinline__ float2 splat(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ Pairs to_pairs(const Mat4& x)
+{
+    Pairs r;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) r.p[q] = make_float2(x.m[2 * q], x.m[2 * q + 1]);
+    return r;
+}
+
+__device__ __forceinline__ Mat4 from_pairs(const Pairs& r)
+{
+    Mat4 x;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        x.m[2 * q] = r.p[q].x;
+        x.m[2 * q + 1] = r.p[q].y;
+    }
+    return x;
+}
+
 // One row step then one column step, in place.  Saves the row-normalised
 // matrix and both factor vectors when the pointers are non-null.
 // Every product and sum is rounded on its own and sums run left to right, as
@@ -35,62 +65,73 @@ __device__ __forceinline__ float sk_inv(float s, float eps) { return (s > eps) ?
 // the column scaling, so their multiplies are not contracted into the column
 // sums); with the correctly rounded reciprocal the result is the reference's
 // bit for bit.
-__device__ __forceinline__ void sk_iteration(float x[16], float eps, float* xr_out, float* rinv_out,
+__device__ __forceinline__ void sk_iteration(Pairs& x, float eps, Pairs* xr_out, float* rinv_out,
                                              float* cinv_out)
 {
-    float ri[4], ci[4];
+    float ri[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float s = __fadd_rn(__fadd_rn(__fadd_rn(x[4 * i], x[4 * i + 1]), x[4 * i + 2]), x[4 * i + 3]);
-        ri[i] = sk_inv(s, eps);
+        const float2 a = x.p[2 * i], b = x.p[2 * i + 1];
+        ri[i] = sk_inv(__fadd_rn(__fadd_rn(__fadd_rn(a.x, a.y), b.x), b.y), eps);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x[4 * i + j] = __fmul_rn(x[4 * i + j], ri[i]);
-    if (xr_out) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) xr_out[e] = x[e];
+    for (int i = 0; i < 4; ++i) {
+        x.p[2 * i] = __fmul2_rn(x.p[2 * i], splat(ri[i]));
+        x.p[2 * i + 1] = __fmul2_rn(x.p[2 * i + 1], splat(ri[i]));
     }
+    if (xr_out) *xr_out = x;
+    // column sums ((x_0j + x_1j) + x_2j) + x_3j, two columns per instruction
+    const float2 c01 = __fadd2_rn(__fadd2_rn(__fadd2_rn(x.p[0], x.p[2]), x.p[4]), x.p[6]);
+    const float2 c23 = __fadd2_rn(__fadd2_rn(__fadd2_rn(x.p[1], x.p[3]), x.p[5]), x.p[7]);
+    const float2 ci01 = make_float2(sk_inv(c01.x, eps), sk_inv(c01.y, eps));
+    const float2 ci23 = make_float2(sk_inv(c23.x, eps), sk_inv(c23.y, eps));
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-        ci[j] = sk_inv(__fadd_rn(__fadd_rn(__fadd_rn(x[j], x[4 + j]), x[8 + j]), x[12 + j]), eps);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) x[4 * i + j] = __fmul_rn(x[4 * i + j], ci[j]);
+    for (int i = 0; i < 4; ++i) {
+        x.p[2 * i] = __fmul2_rn(x.p[2 * i], ci01);
+        x.p[2 * i + 1] = __fmul2_rn(x.p[2 * i + 1], ci23);
+    }
     if (rinv_out) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) rinv_out[i] = ri[i];
     }
     if (cinv_out) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) cinv_out[j] = ci[j];
+        cinv_out[0] = ci01.x;
+        cinv_out[1] = ci01.y;
+        cinv_out[2] = ci23.x;
+        cinv_out[3] = ci23.y;
     }
 }
 
 // Reverse of one iteration.  dy holds d/dy on entry and d/dz on exit.
-__device__ __forceinline__ void sk_iteration_vjp(float dy[16], const float xr[16], const float rinv[4],
+//   column step  dx_ij = (dy_ij - cs_j cinv_j) cinv_j,  cs_j = sum_k dy_kj x_kj
+//                (an FMA chain over k = 0..3)
+//   row step     dz_ij = (dx_ij - rs_i) rinv_i,  rs_i = sum_l dx_il x_il
+//                (an FMA chain over l = 0..3)
+__device__ __forceinline__ void sk_iteration_vjp(Pairs& dy, const Pairs& xr, const float rinv[4],
                                                  const float cinv[4])
 {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        float cs = __fmul_rn(dy[j], xr[j]);
-        cs = __fmaf_rn(dy[4 + j], xr[4 + j], cs);
-        cs = __fmaf_rn(dy[8 + j], xr[8 + j], cs);
-        cs = __fmaf_rn(dy[12 + j], xr[12 + j], cs);
+    for (int h = 0; h < 2; ++h) {  // column pairs (0,1) and (2,3)
+        float2 cs = __fmul2_rn(dy.p[h], xr.p[h]);
+        cs = __ffma2_rn(dy.p[2 + h], xr.p[2 + h], cs);
+        cs = __ffma2_rn(dy.p[4 + h], xr.p[4 + h], cs);
+        cs = __ffma2_rn(dy.p[6 + h], xr.p[6 + h], cs);
+        const float2 ci = make_float2(cinv[2 * h], cinv[2 * h + 1]);
+        const float2 ncs = make_float2(-cs.x, -cs.y);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            dy[4 * i + j] = __fmul_rn(__fmaf_rn(-cs, cinv[j], dy[4 * i + j]), cinv[j]);
+        for (int i = 0; i < 4; ++i) dy.p[2 * i + h] = __fmul2_rn(__ffma2_rn(ncs, ci, dy.p[2 * i + h]), ci);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        float rs = __fmul_rn(dy[4 * i], xr[4 * i]);
-        rs = __fmaf_rn(dy[4 * i + 1], xr[4 * i + 1], rs);
-        rs = __fmaf_rn(dy[4 * i + 2], xr[4 * i + 2], rs);
-        rs = __fmaf_rn(dy[4 * i + 3], xr[4 * i + 3], rs);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dy[4 * i + j] = __fmul_rn(__fsub_rn(dy[4 * i + j], rs), rinv[i]);
+        const float2 a = dy.p[2 * i], b = dy.p[2 * i + 1];
+        const float2 u = xr.p[2 * i], w = xr.p[2 * i + 1];
+        float rs = __fmul_rn(a.x, u.x);
+        rs = __fmaf_rn(a.y, u.y, rs);
+        rs = __fmaf_rn(b.x, w.x, rs);
+        rs = __fmaf_rn(b.y, w.y, rs);
+        const float2 nrs = splat(-rs);
+        dy.p[2 * i] = __fmul2_rn(__fadd2_rn(a, nrs), splat(rinv[i]));
+        dy.p[2 * i + 1] = __fmul2_rn(__fadd2_rn(b, nrs), splat(rinv[i]));
     }
 }
 
