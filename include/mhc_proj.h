@@ -34,8 +34,18 @@ extern "C" {
 
 enum {
     MHC_OK = 0,
-    MHC_ERR_INVALID_VALUE = -1, /* N < 0, or a null pointer with N > 0 */
+    MHC_ERR_INVALID_VALUE = -1, /* N < 0, a null pointer with N > 0, a negative stride or an unknown dtype */
     MHC_ERR_ITERS = -2          /* iteration count outside the supported range */
+};
+
+/* Storage types of the *_ex entry points.  Computation is always fp32: bf16
+ * and fp16 inputs widen exactly, outputs round to nearest even -- the same
+ * bits as converting to fp32, calling the fp32 entry point and converting
+ * back. */
+enum {
+    MHC_DTYPE_F32 = 0,
+    MHC_DTYPE_BF16 = 1,
+    MHC_DTYPE_F16 = 2
 };
 
 /* Largest iteration count sinkhorn_knopp_n4_backward accepts (the
@@ -50,12 +60,29 @@ enum {
 MHC_API int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N,
                          cudaStream_t stream);
 
+/* mhc_birkhoff_proj_n4 on a strided batch of any storage type: matrix k of R
+ * starts at element k * r_stride (its 16 entries row-major and contiguous),
+ * T is written contiguous in the same type.  No reference counterpart: the
+ * reference's wrapper converts R to contiguous fp32 and T back
+ * (solvers_torch.cpp:61,67,82), which this does inside the kernel. */
+MHC_API int mhc_birkhoff_proj_n4_ex(const void* d_R, int64_t r_stride, void* d_T, int dtype,
+                                    float tol, int64_t N, cudaStream_t stream);
+
 /* Backward by the implicit function theorem: D = dL/dR given G = dL/dT and
  * the forward output T.
  * Replaces: void birkhoff_proj_n4_backward(const float* d_G, const float* d_T,
  *           float* d_D, int N, cudaStream_t) -- src/birkhoff_proj_n4.cu:675 */
 MHC_API int mhc_birkhoff_proj_n4_backward(const float* d_G, const float* d_T, float* d_D,
                                   int64_t N, cudaStream_t stream);
+
+/* mhc_birkhoff_proj_n4_backward on strided batches of any storage types:
+ * G (g_dtype, stride g_stride elements) and T (t_dtype, stride t_stride); D
+ * is written contiguous in G's type.  No reference counterpart: the
+ * reference's wrapper converts G and T to contiguous fp32 and D back
+ * (solvers_torch.cpp:128-136,152). */
+MHC_API int mhc_birkhoff_proj_n4_backward_ex(const void* d_G, int64_t g_stride, int g_dtype,
+                                             const void* d_T, int64_t t_stride, int t_dtype,
+                                             void* d_D, int64_t N, cudaStream_t stream);
 
 /* Fixed-iteration Sinkhorn-Knopp on M (= exp(R)): `num_iters` row then
  * column normalisations, a sum s <= 1e-8 giving a zero factor.

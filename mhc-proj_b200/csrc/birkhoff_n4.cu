@@ -38,9 +38,12 @@ enum Stage : int {
 // the output by the pass that finishes the matrix.  The beta = 0 evaluation
 // writes its T as well, for the one exit that comes after a column pass (the
 // alpha = 0 initialisation rejected and beta = 0 already converged).
-template <class Rd, bool kVec>
-__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float* __restrict__ R,
-                                                                    float* __restrict__ Tout, float tol,
+//
+// Elem is the storage type of R and T (fp32, bf16 or fp16; computation is
+// fp32).  Matrix k of R starts at element k * r_stride; T is contiguous.
+template <class Rd, class Elem, bool kVec>
+__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* __restrict__ R, int64_t r_stride,
+                                                                    Elem* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_warp)
 {
     using Prod = typename Rd::P;
@@ -63,7 +66,7 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
     int64_t idx = begin + lane;
     int stage = kIdle;
     if (idx < end) {
-        load_mat<kVec>(R, idx, r);
+        load_elems<Elem, kVec>(R, idx * r_stride, r);
         stage = kEval0;
     } else {
 #pragma unroll
@@ -165,14 +168,14 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
                                : stage;
 
         // T leaves with the pass that produced it.
-        if (s_eval0 || (done && !col)) store_mat<kVec>(Tout, idx, Tn);
+        if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, idx * 16, Tn);
         // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);
         if (want) {
             if (done) {
                 idx = next + __popc(want & ((1u << lane) - 1u));
                 if (idx < end) {
-                    load_mat<kVec>(R, idx, r);
+                    load_elems<Elem, kVec>(R, idx * r_stride, r);
                     stage = kEval0;
                 }
             }
@@ -181,77 +184,143 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const float*
     }
 }
 
-template <class Rd, bool kVec>
-__global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const float* __restrict__ G,
-                                                                      const float* __restrict__ T,
-                                                                      float* __restrict__ D, int64_t N)
+// One thread per matrix.  G and T may have different storage types and batch
+// strides; D is contiguous in G's type (the reference returns D in G's
+// dtype, solvers_torch.cpp:152).
+template <class Rd, class GE, class TE, bool kVec>
+__global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const GE* __restrict__ G, int64_t g_stride,
+                                                                      const TE* __restrict__ T, int64_t t_stride,
+                                                                      GE* __restrict__ D, int64_t N)
 {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
     Mat4 g, t, d;
-    load_mat<kVec>(G, idx, g);
-    load_mat<kVec>(T, idx, t);
+    load_elems<GE, kVec>(G, idx * g_stride, g);
+    load_elems<TE, kVec>(T, idx * t_stride, t);
     ift_backward<Rd>(g, t, d);
-    store_mat<kVec>(D, idx, d);
+    store_elems<GE, kVec>(D, idx * 16, d);
 }
 
-// Resident warps of the forward kernel on the current device.
-static int64_t forward_warp_slots(bool vec)
+// Resident warps of a forward kernel instantiation on the current device.
+template <class Kernel>
+static int64_t forward_warp_slots(Kernel kernel)
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
     int sms = 0, blocks = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    const cudaError_t e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                                    &blocks, birkhoff_fwd_kernel<RefRounding, true>, kNewtonBlock, 0)
-                              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                                    &blocks, birkhoff_fwd_kernel<RefRounding, false>, kNewtonBlock, 0);
-    if (e != cudaSuccess || blocks < 1) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kNewtonBlock, 0) != cudaSuccess || blocks < 1)
+        return 0;
     return static_cast<int64_t>(sms) * blocks * (kNewtonBlock / 32);
 }
 
-}  // namespace mhcp
-
-using namespace mhcp;
-
-extern "C" int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N, cudaStream_t stream)
+template <class Elem, bool kVec>
+static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream)
 {
-    if (N < 0 || (N > 0 && (!d_R || !d_T))) return MHC_ERR_INVALID_VALUE;
-    if (N == 0) return MHC_OK;
-    const bool vec = aligned16(d_R) && aligned16(d_T);
-    const int64_t slots = forward_warp_slots(vec);
-    if (slots <= 0) return static_cast<int>(cudaGetLastError() != cudaSuccess ? cudaGetLastError()
-                                                                                : cudaErrorUnknown);
+    auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec>;
+    const int64_t slots = forward_warp_slots(kernel);
+    if (slots <= 0) {
+        const cudaError_t e = cudaGetLastError();
+        return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
+    }
     // Enough warps to fill the GPU once; each takes an equal contiguous share.
     const int64_t warps = min(ceil_div(N, 32), slots);
     const int64_t per_warp = ceil_div(N, warps);
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
-    if (vec)
-        birkhoff_fwd_kernel<RefRounding, true><<<grid, kNewtonBlock, 0, stream>>>(d_R, d_T, tol, N, per_warp);
-    else
-        birkhoff_fwd_kernel<RefRounding, false><<<grid, kNewtonBlock, 0, stream>>>(d_R, d_T, tol, N, per_warp);
+    kernel<<<grid, kNewtonBlock, 0, stream>>>(static_cast<const Elem*>(R), r_stride, static_cast<Elem*>(T), tol, N,
+                                              per_warp);
     return static_cast<int>(cudaGetLastError());
+}
+
+template <class Elem>
+static int forward_typed(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream)
+{
+    const bool vec = aligned16(R, r_stride, sizeof(Elem)) && aligned16(T);
+    return vec ? launch_forward<Elem, true>(R, r_stride, T, tol, N, stream)
+               : launch_forward<Elem, false>(R, r_stride, T, tol, N, stream);
+}
+
+template <class GE, class TE>
+static int backward_typed(const void* G, int64_t g_stride, const void* T, int64_t t_stride, void* D, int64_t N,
+                          cudaStream_t stream)
+{
+    const int64_t grid = ceil_div(N, kBackwardBlock);
+    const bool vec = aligned16(G, g_stride, sizeof(GE)) && aligned16(T, t_stride, sizeof(TE)) && aligned16(D);
+    const GE* g = static_cast<const GE*>(G);
+    const TE* t = static_cast<const TE*>(T);
+    GE* d = static_cast<GE*>(D);
+    if (vec)
+        birkhoff_bwd_kernel<RefRounding, GE, TE, true><<<grid, kBackwardBlock, 0, stream>>>(g, g_stride, t, t_stride,
+                                                                                            d, N);
+    else
+        birkhoff_bwd_kernel<RefRounding, GE, TE, false><<<grid, kBackwardBlock, 0, stream>>>(g, g_stride, t,
+                                                                                             t_stride, d, N);
+    return static_cast<int>(cudaGetLastError());
+}
+
+template <class GE>
+static int backward_t(const void* G, int64_t g_stride, const void* T, int64_t t_stride, int t_dtype, void* D,
+                      int64_t N, cudaStream_t stream)
+{
+    switch (t_dtype) {
+        case MHC_DTYPE_F32: return backward_typed<GE, float>(G, g_stride, T, t_stride, D, N, stream);
+        case MHC_DTYPE_BF16: return backward_typed<GE, __nv_bfloat16>(G, g_stride, T, t_stride, D, N, stream);
+        case MHC_DTYPE_F16: return backward_typed<GE, __half>(G, g_stride, T, t_stride, D, N, stream);
+        default: return MHC_ERR_INVALID_VALUE;
+    }
+}
+
+static bool valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
+
+}  // namespace mhcp
+
+using namespace mhcp;
+
+extern "C" int mhc_birkhoff_proj_n4_ex(const void* d_R, int64_t r_stride, void* d_T, int dtype, float tol, int64_t N,
+                                       cudaStream_t stream)
+{
+    if (N < 0 || r_stride < 0 || !valid_dtype(dtype) || (N > 0 && (!d_R || !d_T))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    switch (dtype) {
+        case MHC_DTYPE_BF16: return forward_typed<__nv_bfloat16>(d_R, r_stride, d_T, tol, N, stream);
+        case MHC_DTYPE_F16: return forward_typed<__half>(d_R, r_stride, d_T, tol, N, stream);
+        default: return forward_typed<float>(d_R, r_stride, d_T, tol, N, stream);
+    }
+}
+
+extern "C" int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N, cudaStream_t stream)
+{
+    return mhc_birkhoff_proj_n4_ex(d_R, 16, d_T, MHC_DTYPE_F32, tol, N, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_backward_ex(const void* d_G, int64_t g_stride, int g_dtype, const void* d_T,
+                                                int64_t t_stride, int t_dtype, void* d_D, int64_t N,
+                                                cudaStream_t stream)
+{
+    if (N < 0 || g_stride < 0 || t_stride < 0 || !valid_dtype(g_dtype) || !valid_dtype(t_dtype) ||
+        (N > 0 && (!d_G || !d_T || !d_D)))
+        return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    switch (g_dtype) {
+        case MHC_DTYPE_BF16:
+            return backward_t<__nv_bfloat16>(d_G, g_stride, d_T, t_stride, t_dtype, d_D, N, stream);
+        case MHC_DTYPE_F16: return backward_t<__half>(d_G, g_stride, d_T, t_stride, t_dtype, d_D, N, stream);
+        default: return backward_t<float>(d_G, g_stride, d_T, t_stride, t_dtype, d_D, N, stream);
+    }
 }
 
 extern "C" int mhc_birkhoff_proj_n4_backward(const float* d_G, const float* d_T, float* d_D, int64_t N,
                                              cudaStream_t stream)
 {
-    if (N < 0 || (N > 0 && (!d_G || !d_T || !d_D))) return MHC_ERR_INVALID_VALUE;
-    if (N == 0) return MHC_OK;
-    const int64_t grid = ceil_div(N, kBackwardBlock);
-    if (aligned16(d_G) && aligned16(d_T) && aligned16(d_D))
-        birkhoff_bwd_kernel<RefRounding, true><<<grid, kBackwardBlock, 0, stream>>>(d_G, d_T, d_D, N);
-    else
-        birkhoff_bwd_kernel<RefRounding, false><<<grid, kBackwardBlock, 0, stream>>>(d_G, d_T, d_D, N);
-    return static_cast<int>(cudaGetLastError());
+    return mhc_birkhoff_proj_n4_backward_ex(d_G, 16, MHC_DTYPE_F32, d_T, 16, MHC_DTYPE_F32, d_D, N, stream);
 }
 
 extern "C" const char* mhc_status_string(int status)
 {
     switch (status) {
         case MHC_OK: return "success";
-        case MHC_ERR_INVALID_VALUE: return "invalid argument (negative N or null pointer)";
+        case MHC_ERR_INVALID_VALUE: return "invalid argument (negative N or stride, null pointer or unknown dtype)";
         case MHC_ERR_ITERS: return "iteration count outside the supported range";
         default: break;
     }

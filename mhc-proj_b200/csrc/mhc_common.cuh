@@ -7,6 +7,8 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace mhcp {
@@ -67,8 +69,78 @@ __device__ __forceinline__ float pmax4(float a, float b, float c, float d)
     return fmaxf(fmaxf(a, b), fmaxf(c, d));
 }
 
+// ---------------------------------------------------------------------------
+// Element types other than fp32.  A matrix of `Elem` is loaded into fp32
+// registers (bf16 and fp16 widen exactly) and stored back with
+// round-to-nearest-even, the conversions torch's .to() performs, so running
+// on the native type gives the bits of converting to fp32, computing, and
+// converting back.  `off` is the element offset of the matrix's first entry;
+// its 16 entries are row-major and contiguous.  kVec: 16-byte aligned.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+
+template <class Elem>
+__device__ __forceinline__ Elem from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+template <class Elem, bool kVec>
+__device__ __forceinline__ void load_elems(const Elem* __restrict__ base, int64_t off, Mat4& a)
+{
+    if constexpr (sizeof(Elem) == 4) {
+        load_mat<kVec>(reinterpret_cast<const float*>(base) + off, 0, a);
+    } else if constexpr (kVec) {
+        // 16 half-width values = two 16-byte loads
+        const uint4* q = reinterpret_cast<const uint4*>(base + off);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 v = __ldg(q + h);
+            const Elem* e = reinterpret_cast<const Elem*>(&v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a.m[8 * h + k] = to_f32(e[k]);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) a.m[k] = to_f32(base[off + k]);
+    }
+}
+
+template <class Elem, bool kVec>
+__device__ __forceinline__ void store_elems(Elem* __restrict__ base, int64_t off, const Mat4& a)
+{
+    if constexpr (sizeof(Elem) == 4) {
+        store_mat<kVec>(reinterpret_cast<float*>(base) + off, 0, a);
+    } else if constexpr (kVec) {
+        uint4* q = reinterpret_cast<uint4*>(base + off);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint4 v;
+            Elem* e = reinterpret_cast<Elem*>(&v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) e[k] = from_f32<Elem>(a.m[8 * h + k]);
+            __stcs(q + h, v);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) base[off + k] = from_f32<Elem>(a.m[k]);
+    }
+}
+
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// A strided batch takes the 16-byte path when its base and every matrix start
+// are 16-byte aligned.
+inline bool aligned16(const void* p, int64_t stride_elems, int elem_bytes)
+{
+    return aligned16(p) && ((stride_elems * elem_bytes) & 15) == 0;
+}
 
 }  // namespace mhcp

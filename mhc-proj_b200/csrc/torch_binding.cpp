@@ -16,7 +16,10 @@
 // with exp(R)) into the kernels.
 // Differences: kernels run on PyTorch's current stream of the target device
 // (the reference uses cudaStreamPerThread), batch sizes are 64-bit, B = 0 is
-// a no-op, and a failed launch raises RuntimeError.
+// a no-op, and a failed launch raises RuntimeError.  The Newton pair reads
+// fp32/bf16/fp16 CUDA batches with contiguous 4 x 4 matrices in place, at any
+// batch stride, instead of copying them to contiguous fp32 and back; the
+// results are the same bits.
 #include <stdexcept>
 #include <string>
 
@@ -56,9 +59,39 @@ void check_status(int status, const char* what)
 
 cudaStream_t current_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Storage type code of the *_ex entry points, or -1.
+int dtype_code(const torch::Tensor& x)
+{
+    switch (x.scalar_type()) {
+        case torch::kFloat32: return MHC_DTYPE_F32;
+        case torch::kBFloat16: return MHC_DTYPE_BF16;
+        case torch::kFloat16: return MHC_DTYPE_F16;
+        default: return -1;
+    }
+}
+
+// A CUDA batch the kernels read in place: a type they take and contiguous
+// 4 x 4 matrices at any non-negative batch stride.
+bool native_batch(const torch::Tensor& x)
+{
+    return x.is_cuda() && dtype_code(x) >= 0 && x.stride(2) == 1 && x.stride(1) == 4 && x.stride(0) >= 0;
+}
+
 py::dict birkhoff_proj_n4(torch::Tensor R, float tol, const py::kwargs&)
 {
     check_batch(R, "R");
+    if (native_batch(R)) {
+        // fp32/bf16/fp16 at any batch stride: read in place, T in R's type
+        const c10::cuda::CUDAGuard guard(R.device());
+        const int64_t n = R.size(0);
+        torch::Tensor T = torch::empty({n, 4, 4}, R.options());
+        check_status(mhc_birkhoff_proj_n4_ex(R.data_ptr(), R.stride(0), T.data_ptr(), dtype_code(R), tol, n,
+                                             current_stream()),
+                     "birkhoff_proj_n4");
+        py::dict out;
+        out["T"] = T;
+        return out;
+    }
     const auto src = R.options();
     const auto opts = target_options(R);
     R = R.to(opts);
@@ -77,6 +110,17 @@ py::dict birkhoff_proj_n4_backward(torch::Tensor G, torch::Tensor T, const py::k
 {
     check_batch(G, "G");
     check_batch(T, "T", G.size(0));
+    if (native_batch(G) && native_batch(T) && G.device() == T.device()) {
+        const c10::cuda::CUDAGuard guard(G.device());
+        const int64_t n = G.size(0);
+        torch::Tensor D = torch::empty({n, 4, 4}, G.options());
+        check_status(mhc_birkhoff_proj_n4_backward_ex(G.data_ptr(), G.stride(0), dtype_code(G), T.data_ptr(),
+                                                      T.stride(0), dtype_code(T), D.data_ptr(), n, current_stream()),
+                     "birkhoff_proj_n4_backward");
+        py::dict out;
+        out["D"] = D;
+        return out;
+    }
     const auto src = G.options();
     const auto opts = target_options(G);
     G = G.to(opts);

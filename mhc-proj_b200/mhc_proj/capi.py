@@ -16,6 +16,8 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmhcproj
 EXPORTED = (
     "mhc_birkhoff_proj_n4",
     "mhc_birkhoff_proj_n4_backward",
+    "mhc_birkhoff_proj_n4_ex",
+    "mhc_birkhoff_proj_n4_backward_ex",
     "mhc_sinkhorn_knopp_n4",
     "mhc_sinkhorn_knopp_n4_backward",
     "mhc_sinkhorn_knopp_n4_logits",
@@ -23,12 +25,13 @@ EXPORTED = (
     "mhc_status_string",
     "mhc_abi_version",
 )
-_LAUNCHERS = EXPORTED[:6]
+_LAUNCHERS = EXPORTED[:8]
 
 MHC_OK = 0
 MHC_ERR_INVALID_VALUE = -1
 MHC_ERR_ITERS = -2
 MHC_SK_BACKWARD_MAX_ITERS = 20
+MHC_DTYPE_F32, MHC_DTYPE_BF16, MHC_DTYPE_F16 = 0, 1, 2
 
 
 class MhcError(RuntimeError):
@@ -51,6 +54,8 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_backward.argtypes = [vp, vp, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_backward.argtypes = [vp, vp, vp, i64, i32, vp]
+        L.mhc_birkhoff_proj_n4_ex.argtypes = [vp, i64, vp, i32, f32, i64, vp]
+        L.mhc_birkhoff_proj_n4_backward_ex.argtypes = [vp, i64, i32, vp, i64, i32, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
         for f in _LAUNCHERS:
@@ -82,6 +87,16 @@ def birkhoff_proj_n4(R: int, T: int, tol: float, N: int, stream: int = 0) -> Non
 
 def birkhoff_proj_n4_backward(G: int, T: int, D: int, N: int, stream: int = 0) -> None:
     _check(lib().mhc_birkhoff_proj_n4_backward(G, T, D, N, stream), "mhc_birkhoff_proj_n4_backward")
+
+
+def birkhoff_proj_n4_ex(R: int, r_stride: int, T: int, dtype: int, tol: float, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_ex(R, r_stride, T, dtype, tol, N, stream), "mhc_birkhoff_proj_n4_ex")
+
+
+def birkhoff_proj_n4_backward_ex(G: int, g_stride: int, g_dtype: int, T: int, t_stride: int, t_dtype: int,
+                                 D: int, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_backward_ex(G, g_stride, g_dtype, T, t_stride, t_dtype, D, N, stream),
+           "mhc_birkhoff_proj_n4_backward_ex")
 
 
 def sinkhorn_knopp_n4(M: int, T: int, N: int, num_iters: int, stream: int = 0) -> None:
@@ -163,4 +178,40 @@ def sinkhorn_knopp_n4_logits_backward_tensor(G, R, num_iters: int = 20, out=None
 
     D = torch.empty_like(G) if out is None else out
     sinkhorn_knopp_n4_logits_backward(_dev(G, "G"), _dev(R, "R"), _dev(D, "D"), G.shape[0], num_iters, _stream(G))
+    return D
+
+
+def _dtype_code(x) -> int:
+    import torch
+
+    codes = {torch.float32: MHC_DTYPE_F32, torch.bfloat16: MHC_DTYPE_BF16, torch.float16: MHC_DTYPE_F16}
+    if x.dtype not in codes:
+        raise ValueError(f"unsupported dtype {x.dtype}")
+    return codes[x.dtype]
+
+
+def _strided(x, name):
+    if not (x.is_cuda and x.dim() == 3 and tuple(x.shape[1:]) == (4, 4) and x.stride(2) == 1 and x.stride(1) == 4):
+        raise ValueError(f"{name} must be a CUDA (N, 4, 4) tensor with contiguous 4x4 matrices")
+    return x.data_ptr(), x.stride(0), _dtype_code(x)
+
+
+def birkhoff_proj_n4_ex_tensor(R, tol: float = 1e-6):
+    """Newton forward on a strided fp32/bf16/fp16 batch; T contiguous in R's dtype."""
+    import torch
+
+    ptr, stride, dt = _strided(R, "R")
+    T = torch.empty(R.shape, dtype=R.dtype, device=R.device)
+    birkhoff_proj_n4_ex(ptr, stride, T.data_ptr(), dt, tol, R.shape[0], _stream(R))
+    return T
+
+
+def birkhoff_proj_n4_backward_ex_tensor(G, T):
+    """IFT backward on strided batches; D contiguous in G's dtype."""
+    import torch
+
+    gp, gs, gd = _strided(G, "G")
+    tp, ts, td = _strided(T, "T")
+    D = torch.empty(G.shape, dtype=G.dtype, device=G.device)
+    birkhoff_proj_n4_backward_ex(gp, gs, gd, tp, ts, td, D.data_ptr(), G.shape[0], _stream(G))
     return D

@@ -67,3 +67,17 @@ def test_backward_iteration_limit():
 ])
 def test_empty_batch_is_a_no_op(fn, args):
     fn(*args)  # no launch, no error
+
+
+@pytest.mark.parametrize("fn,args", [
+    (capi.birkhoff_proj_n4_ex, (FAKE, -16, FAKE, capi.MHC_DTYPE_F32, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_ex, (FAKE, 16, FAKE, 7, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_ex, (0, 16, FAKE, capi.MHC_DTYPE_BF16, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_backward_ex, (FAKE, 16, 3, FAKE, 16, 0, FAKE, 5)),
+    (capi.birkhoff_proj_n4_backward_ex, (FAKE, 16, 0, FAKE, -1, 0, FAKE, 5)),
+    (capi.birkhoff_proj_n4_backward_ex, (FAKE, 16, 0, FAKE, 16, -2, FAKE, 5)),
+])
+def test_ex_invalid_arguments_rejected(fn, args):
+    with pytest.raises(capi.MhcError) as e:
+        fn(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
