@@ -60,6 +60,15 @@ enum {
 MHC_API int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N,
                          cudaStream_t stream);
 
+/* mhc_birkhoff_proj_n4 that also reports, per matrix, the number of Newton
+ * iterations taken (0 when the initialisation already meets tol, 20 at the
+ * cap) in d_iters[N] and the final gradient l1 norm in d_gnorm[N]; a matrix
+ * with d_gnorm >= tol stopped at the iteration cap.  T is the same as from
+ * mhc_birkhoff_proj_n4.  No reference counterpart: a convergence report the
+ * reference kernel has no way to give. */
+MHC_API int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float tol, int64_t N,
+                                       int32_t* d_iters, float* d_gnorm, cudaStream_t stream);
+
 /* mhc_birkhoff_proj_n4 on a strided batch of any storage type: matrix k of R
  * starts at element k * r_stride (its 16 entries row-major and contiguous),
  * T is written contiguous in the same type.  No reference counterpart: the

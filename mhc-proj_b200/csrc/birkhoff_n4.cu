@@ -41,10 +41,15 @@ enum Stage : int {
 //
 // Elem is the storage type of R and T (fp32, bf16 or fp16; computation is
 // fp32).  Matrix k of R starts at element k * r_stride; T is contiguous.
-template <class Rd, class Elem, bool kVec>
+// kStats: also write, per matrix, the number of Newton iterations taken and
+// the final gradient l1 norm (a separate instantiation; the plain one carries
+// no cost for it).
+template <class Rd, class Elem, bool kVec, bool kStats = false>
 __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* __restrict__ R, int64_t r_stride,
                                                                     Elem* __restrict__ Tout, float tol,
-                                                                    int64_t N, int64_t per_warp)
+                                                                    int64_t N, int64_t per_warp,
+                                                                    int32_t* __restrict__ iters_out = nullptr,
+                                                                    float* __restrict__ gnorm_out = nullptr)
 {
     using Prod = typename Rd::P;
     const int lane = threadIdx.x & 31;
@@ -169,6 +174,12 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
 
         // T leaves with the pass that produced it.
         if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, idx * 16, Tn);
+        if constexpr (kStats) {
+            if (done) {
+                iters_out[idx] = it;
+                gnorm_out[idx] = gn;
+            }
+        }
         // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);
         if (want) {
@@ -214,10 +225,11 @@ static int64_t forward_warp_slots(Kernel kernel)
     return static_cast<int64_t>(sms) * blocks * (kNewtonBlock / 32);
 }
 
-template <class Elem, bool kVec>
-static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream)
+template <class Elem, bool kVec, bool kStats = false>
+static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream,
+                          int32_t* iters = nullptr, float* gnorm = nullptr)
 {
-    auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec>;
+    auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec, kStats>;
     const int64_t slots = forward_warp_slots(kernel);
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
@@ -229,7 +241,7 @@ static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, i
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
     kernel<<<grid, kNewtonBlock, 0, stream>>>(static_cast<const Elem*>(R), r_stride, static_cast<Elem*>(T), tol, N,
-                                              per_warp);
+                                              per_warp, iters, gnorm);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -292,6 +304,16 @@ extern "C" int mhc_birkhoff_proj_n4_ex(const void* d_R, int64_t r_stride, void* 
 extern "C" int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_t N, cudaStream_t stream)
 {
     return mhc_birkhoff_proj_n4_ex(d_R, 16, d_T, MHC_DTYPE_F32, tol, N, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float tol, int64_t N, int32_t* d_iters,
+                                          float* d_gnorm, cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_R || !d_T || !d_iters || !d_gnorm))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    return aligned16(d_R) && aligned16(d_T)
+               ? launch_forward<float, true, true>(d_R, 16, d_T, tol, N, stream, d_iters, d_gnorm)
+               : launch_forward<float, false, true>(d_R, 16, d_T, tol, N, stream, d_iters, d_gnorm);
 }
 
 extern "C" int mhc_birkhoff_proj_n4_backward_ex(const void* d_G, int64_t g_stride, int g_dtype, const void* d_T,

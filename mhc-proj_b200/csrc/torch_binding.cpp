@@ -77,9 +77,34 @@ bool native_batch(const torch::Tensor& x)
     return x.is_cuda() && dtype_code(x) >= 0 && x.stride(2) == 1 && x.stride(1) == 4 && x.stride(0) >= 0;
 }
 
-py::dict birkhoff_proj_n4(torch::Tensor R, float tol, const py::kwargs&)
+// return_stats=True (an optional keyword, ignored-kwargs compatible) adds
+// "iters" (int32, Newton iterations per matrix) and "gnorm" (final gradient
+// l1 norm) to the result, computed for fp32 input.
+py::dict birkhoff_proj_n4_stats(torch::Tensor R, float tol)
+{
+    const auto src = R.options();
+    const auto opts = target_options(R);
+    R = R.to(opts);
+    const c10::cuda::CUDAGuard guard(R.device());
+    R = R.contiguous();
+    const int64_t n = R.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, opts);
+    torch::Tensor it = torch::empty({n}, opts.dtype(torch::kInt32));
+    torch::Tensor gn = torch::empty({n}, opts);
+    check_status(mhc_birkhoff_proj_n4_stats(R.data_ptr<float>(), T.data_ptr<float>(), tol, n, it.data_ptr<int32_t>(),
+                                            gn.data_ptr<float>(), current_stream()),
+                 "birkhoff_proj_n4");
+    py::dict out;
+    out["T"] = T.to(src);
+    out["iters"] = it;
+    out["gnorm"] = gn;
+    return out;
+}
+
+py::dict birkhoff_proj_n4(torch::Tensor R, float tol, const py::kwargs& kwargs)
 {
     check_batch(R, "R");
+    if (kwargs.contains("return_stats") && py::cast<bool>(kwargs["return_stats"])) return birkhoff_proj_n4_stats(R, tol);
     if (native_batch(R)) {
         // fp32/bf16/fp16 at any batch stride: read in place, T in R's type
         const c10::cuda::CUDAGuard guard(R.device());

@@ -18,6 +18,7 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_backward",
     "mhc_birkhoff_proj_n4_ex",
     "mhc_birkhoff_proj_n4_backward_ex",
+    "mhc_birkhoff_proj_n4_stats",
     "mhc_sinkhorn_knopp_n4",
     "mhc_sinkhorn_knopp_n4_backward",
     "mhc_sinkhorn_knopp_n4_logits",
@@ -25,7 +26,7 @@ EXPORTED = (
     "mhc_status_string",
     "mhc_abi_version",
 )
-_LAUNCHERS = EXPORTED[:8]
+_LAUNCHERS = EXPORTED[:9]
 
 MHC_OK = 0
 MHC_ERR_INVALID_VALUE = -1
@@ -56,6 +57,7 @@ def lib() -> ctypes.CDLL:
         L.mhc_sinkhorn_knopp_n4_backward.argtypes = [vp, vp, vp, i64, i32, vp]
         L.mhc_birkhoff_proj_n4_ex.argtypes = [vp, i64, vp, i32, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_backward_ex.argtypes = [vp, i64, i32, vp, i64, i32, vp, i64, vp]
+        L.mhc_birkhoff_proj_n4_stats.argtypes = [vp, vp, f32, i64, vp, vp, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
         for f in _LAUNCHERS:
@@ -87,6 +89,10 @@ def birkhoff_proj_n4(R: int, T: int, tol: float, N: int, stream: int = 0) -> Non
 
 def birkhoff_proj_n4_backward(G: int, T: int, D: int, N: int, stream: int = 0) -> None:
     _check(lib().mhc_birkhoff_proj_n4_backward(G, T, D, N, stream), "mhc_birkhoff_proj_n4_backward")
+
+
+def birkhoff_proj_n4_stats(R: int, T: int, tol: float, N: int, iters: int, gnorm: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_stats(R, T, tol, N, iters, gnorm, stream), "mhc_birkhoff_proj_n4_stats")
 
 
 def birkhoff_proj_n4_ex(R: int, r_stride: int, T: int, dtype: int, tol: float, N: int, stream: int = 0) -> None:

@@ -151,3 +151,23 @@ def test_fused_logits_backward_iteration_limit():
     R = make_logits("normal", 8, seed=15)
     with pytest.raises(ValueError):
         mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(R, R, 21)
+
+
+@pytest.mark.parametrize("kind", ["normal", "wide"])
+def test_convergence_stats(kind):
+    """return_stats=True adds per-matrix Newton iteration counts and final
+    gradient norms; T is unchanged.  A matrix reports gnorm >= tol exactly
+    when it stopped at the 20-iteration cap."""
+    R = make_logits(kind, 1 << 16, seed=21)
+    out = mhc_proj.torch.birkhoff_proj_n4(R, 1e-6, return_stats=True)
+    assert set(out) == {"T", "iters", "gnorm"}
+    assert torch.equal(out["T"], mhc_proj.torch.birkhoff_proj_n4(R, 1e-6)["T"])
+    it, gn = out["iters"], out["gnorm"]
+    assert it.dtype == torch.int32 and int(it.min()) >= 0 and int(it.max()) <= 20
+    capped = gn >= 1e-6
+    assert bool((it[capped] == 20).all())
+    # the reported norm is the l1 norm of the first three column sums minus one
+    c = out["T"].double().sum(1)[:, :3]
+    assert torch.allclose(gn.double(), (c - 1).abs().sum(1), atol=2e-6)
+    if kind == "wide":
+        assert int(capped.sum()) > 0

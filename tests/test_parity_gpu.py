@@ -236,3 +236,23 @@ def test_fused_logits_matches_vanilla_autograd():
     P, dRv = oracle.vanilla_sinkhorn(x, G)
     assert (T - P).abs().max().item() < TOL
     assert (dR - dRv).abs().max().item() < TOL
+
+
+# ---- fuzzing: arbitrary inputs, bit for bit -----------------------------------
+
+from hypothesis import HealthCheck, given, settings, strategies as st  # noqa: E402
+from hypothesis.extra.numpy import arrays  # noqa: E402
+
+_any32 = st.floats(width=32, allow_nan=True, allow_infinity=True, allow_subnormal=True)
+
+
+@settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+@given(R=arrays(np.float32, (96, 4, 4), elements=_any32), G=arrays(np.float32, (96, 4, 4), elements=_any32),
+       tol=st.sampled_from([1e-6, 1e-3, 0.0]))
+def test_fuzz_against_reference(ref, R, G, tol):
+    Rd = torch.from_numpy(R).cuda()
+    Gd = torch.from_numpy(G).cuda()
+    T = capi.birkhoff_proj_n4_tensor(Rd, tol=tol)
+    Tr = ref_forward(ref, Rd, tol)
+    assert bitwise_equal(T, Tr)
+    assert bitwise_equal(capi.birkhoff_proj_n4_backward_tensor(Gd, Tr), ref_backward(ref, Gd, Tr))
