@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
             float dn[4];
             newton_direction<Rd>(p, c, gn, dn);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) d[j] = fresh ? dn[j] : d[j];
-            k = fresh ? 0 : k;
+            for (int j = 0; j < 4; ++j) d[j] = sel(fresh, dn[j], d[j]);
+            k = sel(fresh, 0, k);
             fresh = false;
         }
         const bool col = s_alpha0 || s_skcol;
@@ -101,16 +101,16 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
         float v[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float base = s_skcol ? alpha[j] : beta[j];
+            const float base = sel(s_skcol, alpha[j], beta[j]);
             const float cand = __fmaf_rn(gamma, d[j], beta[j]);
-            const float vj = s_cand ? cand : base;
-            v[j] = s_eval0 ? 0.0f : s_alpha0 ? -0.0f : vj;
+            const float vj = sel(s_cand, cand, base);
+            v[j] = sel(s_eval0, 0.0f, sel(s_alpha0, -0.0f, vj));
         }
         float X[16];
 #pragma unroll
         for (int l = 0; l < 4; ++l)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) X[4 * l + q] = v[q] + (col ? r.m[4 * q + l] : r.m[4 * l + q]);
+            for (int q = 0; q < 4; ++q) X[4 * l + q] = v[q] + (l == q ? r.m[4 * l + q] : sel(col, r.m[4 * q + l], r.m[4 * l + q]));
         float e[16], s[4], lse[4];
         lse_pass(X, e, s, lse);
 
@@ -140,37 +140,35 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
         const bool take_a0 = s_alpha0 && fa < f;
         const bool newbeta = take_a0 || s_skcol;
 #pragma unroll
-        for (int q = 0; q < 6; ++q) p[q] = adopt ? pn[q] : p[q];
+        for (int q = 0; q < 6; ++q) p[q] = sel(adopt, pn[q], p[q]);
 #pragma unroll
-        for (int j = 0; j < 3; ++j) c[j] = adopt ? cn[j] : c[j];
+        for (int j = 0; j < 3; ++j) c[j] = sel(adopt, cn[j], c[j]);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            alpha[j] = adopt ? lse[j] : alpha[j];
+            alpha[j] = sel(adopt, lse[j], alpha[j]);
             const float bj = lse[j] - lse[3];
-            beta[j] = adopt ? v[j] : newbeta ? bj : beta[j];
+            beta[j] = sel(adopt, v[j], sel(newbeta, bj, beta[j]));
         }
-        f = adopt ? fn : f;
-        gn = adopt ? gnn : gn;
+        f = sel(adopt, fn, f);
+        gn = sel(adopt, gnn, gn);
         // the first convergence test after initialisation (:426-431), or the
         // test at the end of a Newton iteration (:490-494)
         const bool check_init = s_evala || (s_alpha0 && !take_a0);
         const bool end_iter = accept || s_skeval;
-        const int it_next = check_init ? 0 : end_iter ? it + 1 : it;
+        const int it_next = sel(check_init, 0, sel(end_iter, it + 1, it));
         const bool converged = (check_init || end_iter) && gn < tol;
         const bool done = converged || (end_iter && it_next == kNewtonMaxIters);
         const bool next_iter = (check_init || end_iter) && !done;
         it = it_next;
         const bool reject_last = s_cand && !accept && k == kLineSearchMaxIters - 1;
-        k = (s_cand && !accept) ? k + 1 : k;
+        k = sel(s_cand && !accept, k + 1, k);
         fresh = next_iter;
-        stage = stage == kIdle ? kIdle
-              : done           ? kIdle
-              : next_iter      ? kCand
-              : s_eval0        ? kAlpha0
-              : take_a0        ? kEvalA
-              : reject_last    ? kSkCol
-              : s_skcol        ? kSkEval
-                               : stage;
+        stage = sel(stage == kIdle || done, static_cast<int>(kIdle),
+                sel(next_iter, static_cast<int>(kCand),
+                sel(s_eval0, static_cast<int>(kAlpha0),
+                sel(take_a0, static_cast<int>(kEvalA),
+                sel(reject_last, static_cast<int>(kSkCol),
+                sel(s_skcol, static_cast<int>(kSkEval), stage))))));
 
         // T leaves with the pass that produced it.
         if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, idx * 16, Tn);

@@ -27,8 +27,8 @@ constexpr float kEpsilon = 1e-8f;
 
 __device__ __forceinline__ float line_step(int k)
 {
-    // gamma in {1, 0.5, 0.1, 0.05, 0.01}
-    return k == 0 ? 1.0f : k == 1 ? 0.5f : k == 2 ? 0.1f : k == 3 ? 0.05f : 0.01f;
+    // gamma in {1, 0.5, 0.1, 0.05, 0.01}, as selects (no jump table)
+    return sel(k == 0, 1.0f, sel(k == 1, 0.5f, sel(k == 2, 0.1f, sel(k == 3, 0.05f, 0.01f))));
 }
 
 // ---------------------------------------------------------------------------
@@ -264,10 +264,10 @@ __device__ __forceinline__ void newton_direction(const float p[6], const float c
     // both candidates are computed and one is selected, so the code has no
     // branch for a warp to diverge on
     const bool fallback = det <= kEpsilon || rho > 1000.0f;
-    d[0] = fallback ? -g0 : __fmul_rn(-y0, rdet);
-    d[1] = fallback ? -g1 : __fmul_rn(-y1, rdet);
-    d[2] = fallback ? -g2 : __fmul_rn(-y2, rdet);
-    d[3] = fallback ? 0.0f : __fmul_rn(-0.0f, rdet);
+    d[0] = sel(fallback, -g0, __fmul_rn(-y0, rdet));
+    d[1] = sel(fallback, -g1, __fmul_rn(-y1, rdet));
+    d[2] = sel(fallback, -g2, __fmul_rn(-y2, rdet));
+    d[3] = sel(fallback, 0.0f, __fmul_rn(-0.0f, rdet));
 }
 
 // ---------------------------------------------------------------------------

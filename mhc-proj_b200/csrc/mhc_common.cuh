@@ -69,6 +69,26 @@ __device__ __forceinline__ float pmax4(float a, float b, float c, float d)
     return fmaxf(fmaxf(a, b), fmaxf(c, d));
 }
 
+// Bitwise select (p ? a : b) as one selp instruction.  Written in PTX so the
+// compiler cannot turn it back into a branch around the computation of an
+// operand: in the per-lane state machines both operands are always computed
+// and lanes must not split over which one is kept.
+__device__ __forceinline__ float sel(bool p, float a, float b)
+{
+    float r;
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %3, 0;\n\tselp.f32 %0, %1, %2, q;\n\t}"
+        : "=f"(r) : "f"(a), "f"(b), "r"(static_cast<unsigned>(p)));
+    return r;
+}
+
+__device__ __forceinline__ int sel(bool p, int a, int b)
+{
+    int r;
+    asm("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %3, 0;\n\tselp.s32 %0, %1, %2, q;\n\t}"
+        : "=r"(r) : "r"(a), "r"(b), "r"(static_cast<unsigned>(p)));
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // Element types other than fp32.  A matrix of `Elem` is loaded into fp32
 // registers (bf16 and fp16 widen exactly) and stored back with
