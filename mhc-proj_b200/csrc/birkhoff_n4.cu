@@ -55,8 +55,16 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
     const int lane = threadIdx.x & 31;
     const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t begin = warp * per_warp;
-    const int64_t end = min(N, begin + per_warp);
-    if (begin >= end) return;  // warp-uniform
+    if (begin >= N) return;  // warp-uniform
+    // The warp's slice, addressed by 32-bit offsets from its first matrix
+    // (per_warp is at most ceil(N / warps) and far below 2^31).
+    const int cnt = static_cast<int>(min(N - begin, per_warp));
+    R += begin * r_stride;
+    Tout += begin * 16;
+    if constexpr (kStats) {
+        iters_out += begin;
+        gnorm_out += begin;
+    }
 
     Mat4 r;                 // logits of the lane's matrix
     float p[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // Gram sums of T at the current point
@@ -68,16 +76,16 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     int k = 0, it = 0;
     bool fresh = false;     // a new Newton iteration starts: take the direction now
-    int64_t idx = begin + lane;
+    int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
-    if (idx < end) {
-        load_elems<Elem, kVec>(R, idx * r_stride, r);
+    if (idx < cnt) {
+        load_elems<Elem, kVec>(R, static_cast<int64_t>(idx) * r_stride, r);
         stage = kEval0;
     } else {
 #pragma unroll
         for (int e2 = 0; e2 < 16; ++e2) r.m[e2] = 0.0f;
     }
-    int64_t next = min(end, begin + 32);
+    int next = min(cnt, 32);
 
     while (__any_sync(kFullMask, stage != kIdle)) {
         const bool s_eval0 = stage == kEval0, s_alpha0 = stage == kAlpha0, s_evala = stage == kEvalA;
@@ -171,7 +179,7 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
                 sel(s_skcol, static_cast<int>(kSkEval), stage))))));
 
         // T leaves with the pass that produced it.
-        if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, idx * 16, Tn);
+        if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, static_cast<int64_t>(idx) * 16, Tn);
         if constexpr (kStats) {
             if (done) {
                 iters_out[idx] = it;
@@ -183,12 +191,12 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
         if (want) {
             if (done) {
                 idx = next + __popc(want & ((1u << lane) - 1u));
-                if (idx < end) {
-                    load_elems<Elem, kVec>(R, idx * r_stride, r);
+                if (idx < cnt) {
+                    load_elems<Elem, kVec>(R, static_cast<int64_t>(idx) * r_stride, r);
                     stage = kEval0;
                 }
             }
-            next = min(end, next + __popc(want));
+            next = min(cnt, next + __popc(want));
         }
     }
 }
@@ -233,8 +241,9 @@ static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, i
         const cudaError_t e = cudaGetLastError();
         return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
     }
-    // Enough warps to fill the GPU once; each takes an equal contiguous share.
-    const int64_t warps = min(ceil_div(N, 32), slots);
+    // Enough warps to fill the GPU once; each takes an equal contiguous share,
+    // small enough for the kernel's 32-bit offsets within a share.
+    const int64_t warps = max(min(ceil_div(N, 32), slots), ceil_div(N, int64_t{1} << 30));
     const int64_t per_warp = ceil_div(N, warps);
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
