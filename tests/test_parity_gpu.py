@@ -256,3 +256,28 @@ def test_fuzz_against_reference(ref, R, G, tol):
     Tr = ref_forward(ref, Rd, tol)
     assert bitwise_equal(T, Tr)
     assert bitwise_equal(capi.birkhoff_proj_n4_backward_tensor(Gd, Tr), ref_backward(ref, Gd, Tr))
+
+
+def test_batch_beyond_int32_element_indexing():
+    """N = 2^27 + 5 matrices (2^31 + 80 elements per tensor): past the point
+    where the reference's 32-bit element index N*16 overflows
+    (birkhoff_proj_n4.cu:510).  Slices at both ends and across the 2^31
+    element boundary must equal separate launches on those slices."""
+    n = (1 << 27) + 5
+    free, _ = torch.cuda.mem_get_info()
+    if free < 5 * n * 64:
+        pytest.skip("needs ~45 GB of free device memory")
+    R = torch.empty(n, 4, 4, device="cuda")
+    for i in range(0, n, 1 << 24):  # fill in chunks to bound the generator's temporaries
+        m = min(1 << 24, n - i)
+        R[i:i + m] = make_logits("normal", m, seed=77 + i // (1 << 24))
+    G = torch.empty_like(R).normal_()
+    T = capi.birkhoff_proj_n4_tensor(R)
+    D = capi.birkhoff_proj_n4_backward_tensor(G, T)
+    edge = (1 << 27) - 1000  # matrix index whose elements straddle 2^31
+    for a, b in [(0, 4096), (edge, edge + 2000), (n - 3000, n)]:
+        Ts = capi.birkhoff_proj_n4_tensor(R[a:b].contiguous())
+        assert bitwise_equal(T[a:b], Ts)
+        assert bitwise_equal(D[a:b], capi.birkhoff_proj_n4_backward_tensor(G[a:b].contiguous(), Ts))
+    del R, G, T, D
+    torch.cuda.empty_cache()
