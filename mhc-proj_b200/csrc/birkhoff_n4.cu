@@ -1,4 +1,6 @@
 // Kernels and C-ABI launchers for the Newton forward and the IFT backward.
+#include <atomic>
+
 #include "birkhoff_n4.cuh"
 #include "mhc_proj.h"
 
@@ -218,25 +220,36 @@ __global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const GE* 
     store_elems<GE, kVec>(D, idx * 16, d);
 }
 
-// Resident warps of a forward kernel instantiation on the current device.
-template <class Kernel>
-static int64_t forward_warp_slots(Kernel kernel)
+// Resident warps of a forward kernel instantiation on the current device,
+// queried once per device and instantiation (so later launches make no extra
+// runtime calls, which also keeps them legal inside stream capture).
+constexpr int kMaxDevices = 64;
+
+template <auto kKernel>
+static int64_t forward_warp_slots()
 {
+    static std::atomic<int64_t> cache[kMaxDevices];  // per instantiation; 0 = not queried yet
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (dev >= 0 && dev < kMaxDevices) {
+        const int64_t hit = cache[dev].load(std::memory_order_relaxed);
+        if (hit > 0) return hit;
+    }
     int sms = 0, blocks = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kNewtonBlock, 0) != cudaSuccess || blocks < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, kNewtonBlock, 0) != cudaSuccess || blocks < 1)
         return 0;
-    return static_cast<int64_t>(sms) * blocks * (kNewtonBlock / 32);
+    const int64_t slots = static_cast<int64_t>(sms) * blocks * (kNewtonBlock / 32);
+    if (dev >= 0 && dev < kMaxDevices) cache[dev].store(slots, std::memory_order_relaxed);
+    return slots;
 }
 
 template <class Elem, bool kVec, bool kStats = false>
 static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream,
                           int32_t* iters = nullptr, float* gnorm = nullptr)
 {
-    auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec, kStats>;
-    const int64_t slots = forward_warp_slots(kernel);
+    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec, kStats>;
+    const int64_t slots = forward_warp_slots<kernel>();
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
         return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);

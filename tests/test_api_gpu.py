@@ -171,3 +171,47 @@ def test_convergence_stats(kind):
     assert torch.allclose(gn.double(), (c - 1).abs().sum(1), atol=2e-6)
     if kind == "wide":
         assert int(capped.sum()) > 0
+
+
+def test_cuda_graph_capture_and_replay():
+    """Forward and backward captured in a CUDA graph replay to the same bits as
+    eager calls (the launchers make no runtime calls that capture forbids
+    once a device has been seen)."""
+    R = make_logits("sigma_mix", 1 << 16, seed=31)
+    G = make_logits("normal", 1 << 16, seed=32)
+    T0 = mhc_proj.torch.birkhoff_proj_n4(R)["T"]
+    D0 = mhc_proj.torch.birkhoff_proj_n4_backward(G, T0)["D"]
+    Rs, Gs = R.clone(), G.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):  # warm-up on the capture stream
+        mhc_proj.torch.birkhoff_proj_n4(Rs)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        T = mhc_proj.torch.birkhoff_proj_n4(Rs)["T"]
+        D = mhc_proj.torch.birkhoff_proj_n4_backward(Gs, T)["D"]
+    Rs.copy_(make_logits("normal", 1 << 16, seed=33))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(T, mhc_proj.torch.birkhoff_proj_n4(Rs)["T"])
+    Rs.copy_(R)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(T, T0) and torch.equal(D, D0)
+
+
+def test_cuda_graph_capture_sinkhorn():
+    """The fused Sinkhorn pair also captures and replays to the eager bits."""
+    R = make_logits("normal", 1 << 14, seed=41)
+    G = make_logits("normal", 1 << 14, seed=42)
+    T0 = mhc_proj.torch.sinkhorn_knopp_n4_logits(R)["T"]
+    D0 = mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(G, R)["D"]
+    Rs, Gs = R.clone(), G.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        T = mhc_proj.torch.sinkhorn_knopp_n4_logits(Rs)["T"]
+        D = mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(Gs, Rs)["D"]
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(T, T0) and torch.equal(D, D0)
