@@ -129,6 +129,44 @@ MHC_API int mhc_sinkhorn_knopp_n4_logits(const float* d_R, float* d_T, int64_t N
 MHC_API int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const float* d_R, float* d_D,
                                                   int64_t N, int num_iters, cudaStream_t stream);
 
+/* The projection fused with its producer, the H_res pre-activation of an
+ * mHC layer: R[k] = alpha * h[k] / rms[k] + b, formed in the kernel's load
+ * with the reference producer's arithmetic before its exponential
+ * (src/utils.cuh:84-93: r_inv = 1 / rms, then (alpha * h) * r_inv + b as one
+ * multiply and one fused multiply-add).  h[k] is 16 consecutive floats at
+ * d_h + k * h_stride -- e.g. columns 8..23 of a [N, 24] projection output,
+ * h_stride = 24; d_rms holds N floats; d_alpha one float and d_b sixteen
+ * (row-major 4x4), all in device memory so that a call needs no host read.
+ * T (contiguous fp32) is the same as mhc_birkhoff_proj_n4 of that R.
+ * No reference counterpart: the reference's producer writes exp(R) to
+ * memory in a kernel of its own (fused_h_activations, src/utils.cuh:96-127). */
+MHC_API int mhc_birkhoff_proj_n4_hres(const float* d_h, int64_t h_stride, const float* d_rms,
+                                      const float* d_alpha, const float* d_b, float* d_T, float tol,
+                                      int64_t N, cudaStream_t stream);
+
+/* Bytes of device workspace that mhc_birkhoff_proj_n4_hres_backward uses
+ * for N matrices on the current device (its per-block partial sums). */
+MHC_API int mhc_birkhoff_proj_n4_hres_backward_workspace(int64_t N, int64_t* bytes);
+
+/* Backward of mhc_birkhoff_proj_n4_hres given G = dL/dT and its output T:
+ * with D = dL/dR (the same bits as mhc_birkhoff_proj_n4_backward),
+ *   dh[k]   = D[k] * alpha / rms[k]        (written at d_dh + k * dh_stride),
+ *   drms[k] = -alpha / rms[k]^2 * sum(D[k] .* h[k]),
+ *   dalpha  = sum_k sum(D[k] .* h[k]) / rms[k],   db = sum_k D[k].
+ * dalpha and db are overwritten (zeros for N = 0), not accumulated.  The
+ * batch sums are deterministic: the same N, workspace size and GPU model
+ * give the same bits.  d_workspace holds workspace_bytes of scratch (any
+ * contents; the size from mhc_birkhoff_proj_n4_hres_backward_workspace, or
+ * less at the cost of fewer blocks, but at least 68 bytes when N > 0) that
+ * the call owns until it completes on `stream`.  No reference counterpart:
+ * the reference has no backward for its producer. */
+MHC_API int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float* d_T, const float* d_h,
+                                               int64_t h_stride, const float* d_rms,
+                                               const float* d_alpha, float* d_dh, int64_t dh_stride,
+                                               float* d_drms, float* d_dalpha, float* d_db, int64_t N,
+                                               void* d_workspace, int64_t workspace_bytes,
+                                               cudaStream_t stream);
+
 /* Human-readable text for a return code of the functions above. */
 MHC_API const char* mhc_status_string(int status);
 

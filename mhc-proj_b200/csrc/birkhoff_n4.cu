@@ -21,6 +21,49 @@ enum Stage : int {
     kIdle = 6,
 };
 
+// Where the forward finds matrix k's logits.  `advance` moves to a warp's
+// first matrix; `load` reads matrix i of the warp's slice (a 32-bit offset).
+//
+// DenseSource: R[k] at R + k * stride, stored as Elem.
+template <class Elem, bool kVec>
+struct DenseSource {
+    const Elem* R;
+    int64_t stride;
+    __device__ __forceinline__ void advance(int64_t k) { R += k * stride; }
+    __device__ __forceinline__ void load(int i, Mat4& r) const
+    {
+        load_elems<Elem, kVec>(R, static_cast<int64_t>(i) * stride, r);
+    }
+};
+
+// HResSource: the H_res pre-activation of the mHC layer formed on load,
+// R[k] = alpha * h[k] / rms[k] + b, with the arithmetic of the reference's
+// producer before its exponential (utils.cuh:84-93: r_inv = 1 / rms, then
+// (alpha * h) * r_inv + b as one multiply and one fused multiply-add).
+// h[k] is 16 consecutive floats at h + k * stride (a column slice of the
+// projection output); alpha is one float and b sixteen, in device memory.
+template <bool kVec>
+struct HResSource {
+    const float* h;
+    int64_t stride;
+    const float* rms;
+    const float* alpha;
+    const float* b;
+    __device__ __forceinline__ void advance(int64_t k)
+    {
+        h += k * stride;
+        rms += k;
+    }
+    __device__ __forceinline__ void load(int i, Mat4& r) const
+    {
+        load_elems<float, kVec>(h, static_cast<int64_t>(i) * stride, r);
+        const float rinv = fast_rcp(__ldg(rms + i));
+        const float a = __ldg(alpha);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r.m[e] = __fmaf_rn(__fmul_rn(a, r.m[e]), rinv, __ldg(b + e));
+    }
+};
+
 // Newton forward, persistent.  Warp w owns matrices [w*per_warp, ...) of the
 // batch.  Each lane runs the reference algorithm (birkhoff_proj_n4.cu:375-499)
 // for one matrix as a state machine, and a lane that finishes stores its T and
@@ -41,14 +84,13 @@ enum Stage : int {
 // writes its T as well, for the one exit that comes after a column pass (the
 // alpha = 0 initialisation rejected and beta = 0 already converged).
 //
-// Elem is the storage type of R and T (fp32, bf16 or fp16; computation is
-// fp32).  Matrix k of R starts at element k * r_stride; T is contiguous.
+// Src supplies the logits (DenseSource or HResSource); Elem is the storage
+// type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
 // kStats: also write, per matrix, the number of Newton iterations taken and
 // the final gradient l1 norm (a separate instantiation; the plain one carries
 // no cost for it).
-template <class Rd, class Elem, bool kVec, bool kStats = false>
-__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* __restrict__ R, int64_t r_stride,
-                                                                    Elem* __restrict__ Tout, float tol,
+template <class Rd, class Src, class Elem, bool kVec, bool kStats = false>
+__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_warp,
                                                                     int32_t* __restrict__ iters_out = nullptr,
                                                                     float* __restrict__ gnorm_out = nullptr)
@@ -61,7 +103,7 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
     // The warp's slice, addressed by 32-bit offsets from its first matrix
     // (per_warp is at most ceil(N / warps) and far below 2^31).
     const int cnt = static_cast<int>(min(N - begin, per_warp));
-    R += begin * r_stride;
+    src.advance(begin);
     Tout += begin * 16;
     if constexpr (kStats) {
         iters_out += begin;
@@ -81,7 +123,7 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
     if (idx < cnt) {
-        load_elems<Elem, kVec>(R, static_cast<int64_t>(idx) * r_stride, r);
+        src.load(idx, r);
         stage = kEval0;
     } else {
 #pragma unroll
@@ -194,7 +236,7 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(const Elem* 
             if (done) {
                 idx = next + __popc(want & ((1u << lane) - 1u));
                 if (idx < cnt) {
-                    load_elems<Elem, kVec>(R, static_cast<int64_t>(idx) * r_stride, r);
+                    src.load(idx, r);
                     stage = kEval0;
                 }
             }
@@ -218,6 +260,93 @@ __global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const GE* 
     load_elems<TE, kVec>(T, idx * t_stride, t);
     ift_backward<Rd>(g, t, d);
     store_elems<GE, kVec>(D, idx * 16, d);
+}
+
+// The H_res backward: the IFT gradient D = dL/dR of each matrix, carried
+// through R = alpha * h / rms + b.  Per matrix, dh = D * (alpha / rms) and
+// drms = -(alpha / rms^2) * sum(D .* h); over the batch, dalpha =
+// sum_k sum(D_k .* h_k) / rms_k and db = sum_k D_k.  The two batch sums are
+// reduced deterministically: each thread accumulates a fixed set of
+// matrices (grid-stride order), each block folds its threads in a fixed
+// tree into kHResPartials floats of `partials`, and hres_reduce_kernel folds
+// the blocks in a fixed order.  The same N on the same GPU model therefore
+// always gives the same bits.
+constexpr int kHResBlock = 256;
+constexpr int kHResPartials = 17;  // db[0..15], dalpha
+
+template <bool kVec>
+__global__ void __launch_bounds__(kHResBlock) birkhoff_hres_bwd_kernel(
+    const float* __restrict__ G, const float* __restrict__ T, const float* __restrict__ h, int64_t h_stride,
+    const float* __restrict__ rms, const float* __restrict__ alpha, float* __restrict__ dh, int64_t dh_stride,
+    float* __restrict__ drms, float* __restrict__ partials, int64_t N)
+{
+    float acc[kHResPartials];
+#pragma unroll
+    for (int q = 0; q < kHResPartials; ++q) acc[q] = 0.0f;
+    const float a = __ldg(alpha);
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < N; idx += step) {
+        Mat4 g, t, d, x;
+        load_elems<float, kVec>(G, idx * 16, g);
+        load_elems<float, kVec>(T, idx * 16, t);
+        ift_backward<RefRounding>(g, t, d);
+        load_elems<float, kVec>(h, idx * h_stride, x);
+        const float rinv = fast_rcp(__ldg(rms + idx));
+        const float s = __fmul_rn(a, rinv);
+        float rows[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int o = 4 * i;
+            rows[i] = __fmaf_rn(d.m[o + 3], x.m[o + 3],
+                      __fmaf_rn(d.m[o + 2], x.m[o + 2], __fmaf_rn(d.m[o + 1], x.m[o + 1], __fmul_rn(d.m[o], x.m[o]))));
+        }
+        const float q = psum4(rows[0], rows[1], rows[2], rows[3]);
+        drms[idx] = -__fmul_rn(__fmul_rn(s, rinv), q);
+        acc[16] = __fmaf_rn(rinv, q, acc[16]);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            acc[e] = __fadd_rn(acc[e], d.m[e]);
+            x.m[e] = __fmul_rn(d.m[e], s);
+        }
+        store_elems<float, kVec>(dh, idx * dh_stride, x);
+    }
+    // Fold the block: butterflies within each warp, then warp 0 over warps.
+    __shared__ float part[kHResBlock / 32][kHResPartials];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int q = 0; q < kHResPartials; ++q) {
+        float v = acc[q];
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFullMask, v, m));
+        if (lane == 0) part[warp][q] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < kHResPartials) {
+        float v = part[0][threadIdx.x];
+#pragma unroll
+        for (int w = 1; w < kHResBlock / 32; ++w) v = __fadd_rn(v, part[w][threadIdx.x]);
+        partials[static_cast<int64_t>(blockIdx.x) * kHResPartials + threadIdx.x] = v;
+    }
+}
+
+// Folds `blocks` rows of kHResPartials partial sums into db[16] and dalpha:
+// warp q takes column q, its lanes stride over the rows, then a butterfly.
+// blocks == 0 writes zeros (the gradient of an empty batch).
+__global__ void __launch_bounds__(32 * kHResPartials) hres_reduce_kernel(const float* __restrict__ partials,
+                                                                            int blocks, float* __restrict__ db,
+                                                                            float* __restrict__ dalpha)
+{
+    const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
+    float v = 0.0f;
+    for (int b = lane; b < blocks; b += 32) v = __fadd_rn(v, partials[static_cast<int64_t>(b) * kHResPartials + q]);
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFullMask, v, m));
+    if (lane == 0) {
+        if (q < 16)
+            db[q] = v;
+        else
+            *dalpha = v;
+    }
 }
 
 // Resident warps of a forward kernel instantiation on the current device,
@@ -244,11 +373,11 @@ static int64_t forward_warp_slots()
     return slots;
 }
 
-template <class Elem, bool kVec, bool kStats = false>
-static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream,
-                          int32_t* iters = nullptr, float* gnorm = nullptr)
+template <class Src, class Elem, bool kVec, bool kStats = false>
+static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters = nullptr,
+                          float* gnorm = nullptr)
 {
-    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Elem, kVec, kStats>;
+    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats>;
     const int64_t slots = forward_warp_slots<kernel>();
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
@@ -260,17 +389,17 @@ static int launch_forward(const void* R, int64_t r_stride, void* T, float tol, i
     const int64_t per_warp = ceil_div(N, warps);
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
-    kernel<<<grid, kNewtonBlock, 0, stream>>>(static_cast<const Elem*>(R), r_stride, static_cast<Elem*>(T), tol, N,
-                                              per_warp, iters, gnorm);
+    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm);
     return static_cast<int>(cudaGetLastError());
 }
 
 template <class Elem>
 static int forward_typed(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream)
 {
+    const Elem* r = static_cast<const Elem*>(R);
     const bool vec = aligned16(R, r_stride, sizeof(Elem)) && aligned16(T);
-    return vec ? launch_forward<Elem, true>(R, r_stride, T, tol, N, stream)
-               : launch_forward<Elem, false>(R, r_stride, T, tol, N, stream);
+    return vec ? launch_forward<DenseSource<Elem, true>, Elem, true>({r, r_stride}, T, tol, N, stream)
+               : launch_forward<DenseSource<Elem, false>, Elem, false>({r, r_stride}, T, tol, N, stream);
 }
 
 template <class GE, class TE>
@@ -303,6 +432,45 @@ static int backward_t(const void* G, int64_t g_stride, const void* T, int64_t t_
     }
 }
 
+// Blocks of the H_res backward: one wave of resident blocks, at most one per
+// 256 matrices, and at most `cap` (the rows the caller's partial-sum
+// storage holds).
+static int hres_backward_blocks(int64_t N, int64_t cap)
+{
+    static std::atomic<int64_t> cache[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    int64_t wave = (dev >= 0 && dev < kMaxDevices) ? cache[dev].load(std::memory_order_relaxed) : 0;
+    if (wave <= 0) {
+        int sms = 0, per_sm = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, birkhoff_hres_bwd_kernel<true>, kHResBlock, 0) !=
+                cudaSuccess ||
+            per_sm < 1)
+            return -1;
+        wave = static_cast<int64_t>(sms) * per_sm;
+        if (dev >= 0 && dev < kMaxDevices) cache[dev].store(wave, std::memory_order_relaxed);
+    }
+    return static_cast<int>(max(int64_t{0}, min(min(ceil_div(N, kHResBlock), wave), cap)));
+}
+
+static int hres_backward_launch(const float* G, const float* T, const float* h, int64_t h_stride, const float* rms,
+                                const float* alpha, float* dh, int64_t dh_stride, float* drms, float* dalpha,
+                                float* db, int64_t N, float* partials, int blocks, cudaStream_t stream)
+{
+    if (blocks > 0) {
+        const bool vec = aligned16(G) && aligned16(T) && aligned16(h, h_stride, 4) && aligned16(dh, dh_stride, 4);
+        if (vec)
+            birkhoff_hres_bwd_kernel<true><<<blocks, kHResBlock, 0, stream>>>(G, T, h, h_stride, rms, alpha, dh,
+                                                                              dh_stride, drms, partials, N);
+        else
+            birkhoff_hres_bwd_kernel<false><<<blocks, kHResBlock, 0, stream>>>(G, T, h, h_stride, rms, alpha, dh,
+                                                                               dh_stride, drms, partials, N);
+    }
+    hres_reduce_kernel<<<1, 32 * kHResPartials, 0, stream>>>(partials, blocks, db, dalpha);
+    return static_cast<int>(cudaGetLastError());
+}
+
 static bool valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
 
 }  // namespace mhcp
@@ -332,8 +500,10 @@ extern "C" int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float to
     if (N < 0 || (N > 0 && (!d_R || !d_T || !d_iters || !d_gnorm))) return MHC_ERR_INVALID_VALUE;
     if (N == 0) return MHC_OK;
     return aligned16(d_R) && aligned16(d_T)
-               ? launch_forward<float, true, true>(d_R, 16, d_T, tol, N, stream, d_iters, d_gnorm)
-               : launch_forward<float, false, true>(d_R, 16, d_T, tol, N, stream, d_iters, d_gnorm);
+               ? launch_forward<DenseSource<float, true>, float, true, true>({d_R, 16}, d_T, tol, N, stream, d_iters,
+                                                                             d_gnorm)
+               : launch_forward<DenseSource<float, false>, float, false, true>({d_R, 16}, d_T, tol, N, stream,
+                                                                               d_iters, d_gnorm);
 }
 
 extern "C" int mhc_birkhoff_proj_n4_backward_ex(const void* d_G, int64_t g_stride, int g_dtype, const void* d_T,
@@ -356,6 +526,52 @@ extern "C" int mhc_birkhoff_proj_n4_backward(const float* d_G, const float* d_T,
                                              cudaStream_t stream)
 {
     return mhc_birkhoff_proj_n4_backward_ex(d_G, 16, MHC_DTYPE_F32, d_T, 16, MHC_DTYPE_F32, d_D, N, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_hres(const float* d_h, int64_t h_stride, const float* d_rms,
+                                         const float* d_alpha, const float* d_b, float* d_T, float tol, int64_t N,
+                                         cudaStream_t stream)
+{
+    if (N < 0 || h_stride < 0 || (N > 0 && (!d_h || !d_rms || !d_alpha || !d_b || !d_T)))
+        return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    const HResSource<true> vs{d_h, h_stride, d_rms, d_alpha, d_b};
+    const HResSource<false> ss{d_h, h_stride, d_rms, d_alpha, d_b};
+    return aligned16(d_h, h_stride, 4) && aligned16(d_T)
+               ? launch_forward<HResSource<true>, float, true>(vs, d_T, tol, N, stream)
+               : launch_forward<HResSource<false>, float, false>(ss, d_T, tol, N, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_hres_backward_workspace(int64_t N, int64_t* bytes)
+{
+    if (N < 0 || !bytes) return MHC_ERR_INVALID_VALUE;
+    const int blocks = hres_backward_blocks(N, int64_t{1} << 30);
+    if (blocks < 0) {
+        const cudaError_t e = cudaGetLastError();
+        return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
+    }
+    *bytes = static_cast<int64_t>(max(blocks, 1)) * kHResPartials * static_cast<int64_t>(sizeof(float));
+    return MHC_OK;
+}
+
+extern "C" int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float* d_T, const float* d_h,
+                                                  int64_t h_stride, const float* d_rms, const float* d_alpha,
+                                                  float* d_dh, int64_t dh_stride, float* d_drms, float* d_dalpha,
+                                                  float* d_db, int64_t N, void* d_workspace,
+                                                  int64_t workspace_bytes, cudaStream_t stream)
+{
+    if (N < 0 || h_stride < 0 || dh_stride < 0 || !d_dalpha || !d_db || workspace_bytes < 0 ||
+        (N > 0 && (!d_G || !d_T || !d_h || !d_rms || !d_alpha || !d_dh || !d_drms || !d_workspace)))
+        return MHC_ERR_INVALID_VALUE;
+    const int64_t rows = workspace_bytes / (kHResPartials * static_cast<int64_t>(sizeof(float)));
+    const int blocks = hres_backward_blocks(N, rows);
+    if (blocks < 0) {
+        const cudaError_t e = cudaGetLastError();
+        return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
+    }
+    if (N > 0 && blocks == 0) return MHC_ERR_INVALID_VALUE;  // workspace smaller than one row
+    return hres_backward_launch(d_G, d_T, d_h, h_stride, d_rms, d_alpha, d_dh, dh_stride, d_drms, d_dalpha, d_db, N,
+                                static_cast<float*>(d_workspace), blocks, stream);
 }
 
 extern "C" const char* mhc_status_string(int status)

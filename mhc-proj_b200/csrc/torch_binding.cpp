@@ -11,9 +11,10 @@
 //     dtype/device; the backward converts T to G's dtype/device;
 //   - sinkhorn_knopp_n4_backward with max_iter > 20 raises ValueError;
 //   - extra keyword arguments are accepted and ignored.
-// Two functions have no reference counterpart: sinkhorn_knopp_n4_logits and
-// its backward take the logits R and fuse exp(R) (and, backward, the product
-// with exp(R)) into the kernels.
+// Functions with no reference counterpart: sinkhorn_knopp_n4_logits and its
+// backward take the logits R and fuse exp(R) (and, backward, the product with
+// exp(R)) into the kernels; birkhoff_proj_n4_hres and its backward fuse the
+// mHC layer's H_res pre-activation into the projection.
 // Differences: kernels run on PyTorch's current stream of the target device
 // (the reference uses cudaStreamPerThread), batch sizes are 64-bit, B = 0 is
 // a no-op, and a failed launch raises RuntimeError.  The Newton pair reads
@@ -248,6 +249,112 @@ py::dict sinkhorn_knopp_n4_logits_backward(torch::Tensor G, torch::Tensor R, int
     return out;
 }
 
+// The projection fused with its producer, the H_res pre-activation of an
+// mHC layer, R = alpha_res * h_res / rms + b_res (no reference counterpart:
+// the reference's producer, fused_h_activations in src/utils.cuh:50-127,
+// writes exp(R) in a kernel of its own and has no backward).
+//   h_res: B x 16 or B x 4 x 4, e.g. a column slice H_proj_concat[:, 8:24],
+//          read in place when it is fp32 CUDA with contiguous matrices;
+//   rms: B elements; alpha_res: a number or a one-element tensor; b_res: 16
+//   elements.  Everything is converted to fp32 on h_res's CUDA device (the
+//   current device for a CPU h_res); results return in the inputs' dtypes
+//   and devices.
+struct HResInputs {
+    torch::Tensor h, rms, alpha, b;
+    int64_t n;
+};
+
+HResInputs hres_inputs(torch::Tensor h, torch::Tensor rms, const py::object& alpha, torch::Tensor b)
+{
+    const bool flat = h.dim() == 2 && h.size(1) == 16;
+    const bool mat = h.dim() == 3 && h.size(1) == 4 && h.size(2) == 4;
+    if (!flat && !mat) throw std::runtime_error("h_res must be a tensor of size B x 16 or B x 4 x 4");
+    const int64_t n = h.size(0);
+    if (rms.numel() != n) throw std::runtime_error("rms must have B elements");
+    if (b.defined() && b.numel() != 16) throw std::runtime_error("b_res must have 16 elements");
+    const bool alpha_number = py::isinstance<py::float_>(alpha) || py::isinstance<py::int_>(alpha);
+    if (!alpha_number && py::cast<torch::Tensor>(alpha).numel() != 1)
+        throw std::runtime_error("alpha_res must be a number or a one-element tensor");
+    const auto opts = target_options(h);
+    HResInputs in;
+    in.n = n;
+    in.h = h.to(opts);
+    const bool dense = in.h.stride(-1) == 1 && (flat || in.h.stride(1) == 4) && in.h.stride(0) >= 0;
+    if (!dense) in.h = in.h.contiguous();
+    in.rms = rms.to(opts).contiguous().reshape({n});
+    if (b.defined()) in.b = b.to(opts).contiguous().reshape({16});  // the backward needs no b
+    if (alpha_number)
+        in.alpha = torch::full({1}, py::cast<double>(alpha), opts);
+    else
+        in.alpha = py::cast<torch::Tensor>(alpha).to(opts).contiguous().reshape({1});
+    return in;
+}
+
+py::dict birkhoff_proj_n4_hres(torch::Tensor h_res, torch::Tensor rms, py::object alpha_res, torch::Tensor b_res,
+                               float tol, const py::kwargs&)
+{
+    const auto src = h_res.options();
+    HResInputs in = hres_inputs(h_res, rms, alpha_res, b_res);
+    const c10::cuda::CUDAGuard guard(in.h.device());
+    torch::Tensor T = torch::empty({in.n, 4, 4}, in.h.options());
+    check_status(mhc_birkhoff_proj_n4_hres(in.h.data_ptr<float>(), in.h.stride(0), in.rms.data_ptr<float>(),
+                                           in.alpha.data_ptr<float>(), in.b.data_ptr<float>(), T.data_ptr<float>(),
+                                           tol, in.n, current_stream()),
+                 "birkhoff_proj_n4_hres");
+    py::dict out;
+    out["T"] = T.to(src);
+    return out;
+}
+
+// Gradients of sum(G .* T) with T = birkhoff_proj_n4_hres(h_res, rms,
+// alpha_res, b_res): "d_h_res" (shaped like h_res), "d_rms" (like rms),
+// "d_alpha_res" (one element; 0-d for a number) and "d_b_res" (like b_res
+// when given, else 4 x 4).  T is the forward's output.
+py::dict birkhoff_proj_n4_hres_backward(torch::Tensor G, torch::Tensor T, torch::Tensor h_res, torch::Tensor rms,
+                                        py::object alpha_res, const py::kwargs& kwargs)
+{
+    check_batch(G, "G");
+    check_batch(T, "T", G.size(0));
+    if (h_res.size(0) != G.size(0)) throw std::runtime_error("h_res must have the batch size of G");
+    const auto h_src = h_res.options();
+    const auto rms_src = rms.options();
+    HResInputs in = hres_inputs(h_res, rms, alpha_res, torch::Tensor());
+    const auto opts = in.h.options();
+    const c10::cuda::CUDAGuard guard(in.h.device());
+    G = G.to(opts).contiguous();
+    T = T.to(opts).contiguous();
+    torch::Tensor dh = torch::empty({in.n, 16}, opts);
+    torch::Tensor drms = torch::empty({in.n}, opts);
+    torch::Tensor dalpha = torch::empty({1}, opts);
+    torch::Tensor db = torch::empty({16}, opts);
+    int64_t ws_bytes = 0;
+    check_status(mhc_birkhoff_proj_n4_hres_backward_workspace(in.n, &ws_bytes), "birkhoff_proj_n4_hres_backward");
+    torch::Tensor ws = torch::empty({(ws_bytes + 3) / 4}, opts);
+    check_status(mhc_birkhoff_proj_n4_hres_backward(G.data_ptr<float>(), T.data_ptr<float>(), in.h.data_ptr<float>(),
+                                                    in.h.stride(0), in.rms.data_ptr<float>(),
+                                                    in.alpha.data_ptr<float>(), dh.data_ptr<float>(), 16,
+                                                    drms.data_ptr<float>(), dalpha.data_ptr<float>(),
+                                                    db.data_ptr<float>(), in.n, ws.data_ptr(), ws.numel() * 4,
+                                                    current_stream()),
+                 "birkhoff_proj_n4_hres_backward");
+    py::dict out;
+    out["d_h_res"] = dh.reshape(h_res.sizes()).to(h_src);
+    out["d_rms"] = drms.reshape(rms.sizes()).to(rms_src);
+    if (py::isinstance<py::float_>(alpha_res) || py::isinstance<py::int_>(alpha_res)) {
+        out["d_alpha_res"] = dalpha.reshape({});
+    } else {
+        const torch::Tensor a = py::cast<torch::Tensor>(alpha_res);
+        out["d_alpha_res"] = dalpha.reshape(a.sizes()).to(a.options());
+    }
+    if (kwargs.contains("b_res")) {
+        const torch::Tensor b = py::cast<torch::Tensor>(kwargs["b_res"]);
+        out["d_b_res"] = db.reshape(b.sizes()).to(b.options());
+    } else {
+        out["d_b_res"] = db.reshape({4, 4});
+    }
+    return out;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_internal, m)
@@ -268,4 +375,10 @@ PYBIND11_MODULE(_internal, m)
     m_torch.def("sinkhorn_knopp_n4_logits_backward", &sinkhorn_knopp_n4_logits_backward, py::arg("G"),
                 py::arg("R"), py::arg("max_iter") = 20,
                 "Gradient with respect to R of Sinkhorn-Knopp on exp(R), in one kernel");
+    m_torch.def("birkhoff_proj_n4_hres", &birkhoff_proj_n4_hres, py::arg("h_res"), py::arg("rms"),
+                py::arg("alpha_res"), py::arg("b_res"), py::arg("tol") = 1e-6,
+                "Projection of R = alpha_res * h_res / rms + b_res, formed in the kernel's load");
+    m_torch.def("birkhoff_proj_n4_hres_backward", &birkhoff_proj_n4_hres_backward, py::arg("G"), py::arg("T"),
+                py::arg("h_res"), py::arg("rms"), py::arg("alpha_res"),
+                "Gradients of birkhoff_proj_n4_hres with respect to h_res, rms, alpha_res and b_res");
 }

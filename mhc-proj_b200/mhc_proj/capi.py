@@ -23,10 +23,13 @@ EXPORTED = (
     "mhc_sinkhorn_knopp_n4_backward",
     "mhc_sinkhorn_knopp_n4_logits",
     "mhc_sinkhorn_knopp_n4_logits_backward",
+    "mhc_birkhoff_proj_n4_hres",
+    "mhc_birkhoff_proj_n4_hres_backward_workspace",
+    "mhc_birkhoff_proj_n4_hres_backward",
     "mhc_status_string",
     "mhc_abi_version",
 )
-_LAUNCHERS = EXPORTED[:9]
+_LAUNCHERS = EXPORTED[:-2]
 
 MHC_OK = 0
 MHC_ERR_INVALID_VALUE = -1
@@ -60,6 +63,10 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_stats.argtypes = [vp, vp, f32, i64, vp, vp, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
+        L.mhc_birkhoff_proj_n4_hres.argtypes = [vp, i64, vp, vp, vp, vp, f32, i64, vp]
+        L.mhc_birkhoff_proj_n4_hres_backward_workspace.argtypes = [i64, ctypes.POINTER(i64)]
+        L.mhc_birkhoff_proj_n4_hres_backward.argtypes = [vp, vp, vp, i64, vp, vp, vp, i64, vp, vp, vp, i64, vp,
+                                                         i64, vp]
         for f in _LAUNCHERS:
             getattr(L, f).restype = ctypes.c_int
         L.mhc_status_string.argtypes = [ctypes.c_int]
@@ -120,6 +127,28 @@ def sinkhorn_knopp_n4_logits(R: int, T: int, N: int, num_iters: int, stream: int
 def sinkhorn_knopp_n4_logits_backward(G: int, R: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:
     _check(lib().mhc_sinkhorn_knopp_n4_logits_backward(G, R, D, N, num_iters, stream),
            "mhc_sinkhorn_knopp_n4_logits_backward")
+
+
+def birkhoff_proj_n4_hres(h: int, h_stride: int, rms: int, alpha: int, b: int, T: int, tol: float, N: int,
+                          stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_hres(h, h_stride, rms, alpha, b, T, tol, N, stream),
+           "mhc_birkhoff_proj_n4_hres")
+
+
+def birkhoff_proj_n4_hres_backward_workspace(N: int) -> int:
+    """Bytes of workspace mhc_birkhoff_proj_n4_hres_backward uses for N matrices on the current device."""
+    out = ctypes.c_int64(0)
+    _check(lib().mhc_birkhoff_proj_n4_hres_backward_workspace(N, ctypes.byref(out)),
+           "mhc_birkhoff_proj_n4_hres_backward_workspace")
+    return out.value
+
+
+def birkhoff_proj_n4_hres_backward(G: int, T: int, h: int, h_stride: int, rms: int, alpha: int, dh: int,
+                                   dh_stride: int, drms: int, dalpha: int, db: int, N: int, workspace: int,
+                                   workspace_bytes: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_hres_backward(G, T, h, h_stride, rms, alpha, dh, dh_stride, drms, dalpha, db,
+                                                     N, workspace, workspace_bytes, stream),
+           "mhc_birkhoff_proj_n4_hres_backward")
 
 
 # --- tensor conveniences ---------------------------------------------------
@@ -221,3 +250,52 @@ def birkhoff_proj_n4_backward_ex_tensor(G, T):
     D = torch.empty(G.shape, dtype=G.dtype, device=G.device)
     birkhoff_proj_n4_backward_ex(gp, gs, gd, tp, ts, td, D.data_ptr(), G.shape[0], _stream(G))
     return D
+
+
+def _hres_inputs(h, rms, alpha, b):
+    """Pointers and the batch stride of the H_res producer's inputs: h (N, 16)
+    or (N, 4, 4) fp32 CUDA with each matrix's 16 entries contiguous (a column
+    slice of a wider projection output is fine), rms (N,), alpha one element,
+    b 16 elements, all contiguous fp32 on h's device."""
+    import torch
+
+    n = h.shape[0]
+    flat_ok = h.dim() == 2 and h.shape[1] == 16 and h.stride(1) == 1
+    mat_ok = h.dim() == 3 and tuple(h.shape[1:]) == (4, 4) and h.stride(2) == 1 and h.stride(1) == 4
+    if not (h.is_cuda and h.dtype == torch.float32 and (flat_ok or mat_ok)):
+        raise ValueError("h must be a float32 CUDA tensor of shape (N, 16) or (N, 4, 4) with contiguous matrices")
+    for x, name, numel in ((rms, "rms", n), (alpha, "alpha", 1), (b, "b", 16)):
+        if not (x.device == h.device and x.dtype == torch.float32 and x.is_contiguous() and x.numel() == numel):
+            raise ValueError(f"{name} must be a contiguous float32 tensor of {numel} elements on h's device")
+    return h.data_ptr(), h.stride(0), rms.data_ptr(), alpha.data_ptr(), b.data_ptr()
+
+
+def birkhoff_proj_n4_hres_tensor(h, rms, alpha, b, tol: float = 1e-6):
+    """Projection of R = alpha * h / rms + b formed in the kernel's load; T is (N, 4, 4) fp32."""
+    import torch
+
+    hp, hs, rp, ap, bp = _hres_inputs(h, rms, alpha, b)
+    T = torch.empty(h.shape[0], 4, 4, dtype=torch.float32, device=h.device)
+    birkhoff_proj_n4_hres(hp, hs, rp, ap, bp, T.data_ptr(), tol, h.shape[0], _stream(h))
+    return T
+
+
+def birkhoff_proj_n4_hres_backward_tensor(G, T, h, rms, alpha, dh=None):
+    """Gradients (dh, drms, dalpha, db) of the fused producer + projection.  dh
+    is (N, 16) fp32, or written into the given tensor (same layout rules as h)."""
+    import torch
+
+    hp, hs, rp, ap, _ = _hres_inputs(h, rms, alpha, torch.empty(16, device=h.device))
+    n = h.shape[0]
+    if dh is None:
+        dh = torch.empty(n, 16, dtype=torch.float32, device=h.device)
+    dhp, dhs, _, _, _ = _hres_inputs(dh, rms, alpha, torch.empty(16, device=h.device))
+    drms = torch.empty(n, dtype=torch.float32, device=h.device)
+    dalpha = torch.empty((), dtype=torch.float32, device=h.device)
+    db = torch.empty(4, 4, dtype=torch.float32, device=h.device)
+    with torch.cuda.device(h.device):
+        ws = torch.empty(max(birkhoff_proj_n4_hres_backward_workspace(n), 4) // 4, dtype=torch.float32,
+                         device=h.device)
+    birkhoff_proj_n4_hres_backward(_dev(G, "G"), _dev(T, "T"), hp, hs, rp, ap, dhp, dhs, drms.data_ptr(),
+                                   dalpha.data_ptr(), db.data_ptr(), n, ws.data_ptr(), ws.numel() * 4, _stream(h))
+    return dh, drms, dalpha, db

@@ -96,3 +96,64 @@ class MHCSinkhornN4(nn.Module):
         if x.ndim < 2 or in_shape[-1] != 4 or in_shape[-2] != 4:
             raise ValueError("x must be a tensor of size B x 4 x 4")
         return MHCSinkhornN4Function.apply(x, self.max_iter)
+
+
+class MHCProjectionN4HResFunction(torch.autograd.Function):
+    """T = birkhoff_proj_n4(alpha_res * h_res / rms + b_res), the H_res
+    pre-activation formed in the projection's load; gradients for all four
+    inputs from one fused backward kernel plus a deterministic batch
+    reduction.  h_res: (..., 16) or (..., 4, 4); rms: (...); alpha_res: a
+    one-element tensor; b_res: 16 elements.  Returns (..., 4, 4)."""
+
+    @staticmethod
+    def forward(ctx, h_res, rms, alpha_res, b_res, tol=1e-6):
+        lead = rms.shape
+        h2 = h_res.reshape(-1, 16)
+        T = _internal.torch.birkhoff_proj_n4_hres(h2, rms.reshape(-1), alpha_res, b_res, tol)["T"]
+        ctx.save_for_backward(T, h2, rms, alpha_res, b_res)
+        ctx.h_shape = h_res.shape
+        ctx.set_materialize_grads(False)
+        return T.view(*lead, 4, 4)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if grad_output is None or not any(ctx.needs_input_grad[:4]):
+            return None, None, None, None, None
+        T, h2, rms, alpha_res, b_res = ctx.saved_tensors
+        g = _internal.torch.birkhoff_proj_n4_hres_backward(grad_output.reshape(-1, 4, 4), T, h2, rms.reshape(-1),
+                                                           alpha_res, b_res=b_res)
+        need = ctx.needs_input_grad
+        return (g["d_h_res"].view(ctx.h_shape) if need[0] else None,
+                g["d_rms"].view(rms.shape) if need[1] else None,
+                g["d_alpha_res"] if need[2] else None,
+                g["d_b_res"] if need[3] else None,
+                None)
+
+
+class MHCProjectionN4HRes(nn.Module):
+    """Projection fused with the mHC layer's H_res pre-activation (no
+    reference counterpart; the reference's producer is fused_h_activations,
+    src/utils.cuh:50-127, a separate kernel that writes exp(R)).
+
+    forward(h_res, rms, alpha_res, b_res) with h_res (..., 16) -- e.g. the
+    column slice H_proj_concat[..., 8:24] -- or (..., 4, 4), rms (...),
+    alpha_res a number or one-element tensor, b_res 16 elements; returns
+    (..., 4, 4), the same T as MHCProjectionN4 applied to
+    alpha_res * h_res / rms + b_res computed with the producer's arithmetic."""
+
+    def __init__(self, tol=1e-6):
+        super().__init__()
+        self.tol = tol
+
+    def forward(self, h_res, rms, alpha_res, b_res):
+        if h_res.shape[-1] == 16:
+            lead = h_res.shape[:-1]
+        elif h_res.ndim >= 2 and h_res.shape[-2:] == (4, 4):
+            lead = h_res.shape[:-2]
+        else:
+            raise ValueError("h_res must be a tensor of size ... x 16 or ... x 4 x 4")
+        if tuple(rms.shape) != tuple(lead):
+            raise ValueError("rms must have the leading shape of h_res")
+        if not torch.is_tensor(alpha_res):
+            alpha_res = torch.tensor(float(alpha_res), dtype=torch.float32, device=h_res.device)
+        return MHCProjectionN4HResFunction.apply(h_res, rms, alpha_res, b_res, self.tol)

@@ -3,7 +3,9 @@
 ctypes bindings over ``liboracle.so`` (the CPU restatement of the reference
 algorithms in ``birkhoff_oracle.c``) and over ``_ref/libmhcref.so`` (the
 reference's own CUDA kernels compiled unmodified from their source files,
-``ref_shim.cu`` giving them extern "C" names).
+``ref_shim.cu`` giving them extern "C" names), and over
+``_ref/libmhcref_hres.so`` (the reference's H_res producer from
+src/utils.cuh, ``ref_hres_shim.cu``).
 
 Only the tests, the smoke check and the CPU-baseline leg of the benchmark use
 this package, always as the checker or the timed baseline, never as a product
@@ -164,3 +166,79 @@ class RefCuda:
     def sinkhorn_knopp_n4_backward(self, G, M, D, N, iters, stream):
         self._check(self.lib.ref_sinkhorn_knopp_n4_backward(G, M, D, int(N), int(iters), stream),
                     "sinkhorn_knopp_n4_backward")
+
+
+# --- the mHC layer's H_res producer ---------------------------------------
+
+REF_HRES_LIB = os.path.join(_HERE, "_ref", "libmhcref_hres.so")
+
+
+def hres_logits(h, rms, alpha, b):
+    """The H_res pre-activation R = alpha * h / rms + b of the reference's
+    producer (src/utils.cuh:84-93), in float64 from the float32 inputs: h
+    (N, 16), rms (N,), alpha a number, b (16,).  Returns (N, 4, 4) float64.
+    The kernels round this to float32 in two steps (the product alpha * h,
+    then a fused multiply-add with 1 / rms); the float64 value bounds them."""
+    h = np.asarray(h, dtype=np.float64).reshape(-1, 16)
+    rms = np.asarray(rms, dtype=np.float64).reshape(-1, 1)
+    b = np.asarray(b, dtype=np.float64).reshape(1, 16)
+    return (float(alpha) * h / rms + b).reshape(-1, 4, 4)
+
+
+def hres_backward_chain(D, h, rms, alpha):
+    """Chain rule through R = alpha * h / rms + b, in float64: given D = dL/dR
+    (N, 4, 4), returns (dh (N, 16), drms (N,), dalpha, db (4, 4)) with
+    dh = D alpha / rms, drms = -alpha / rms^2 sum(D h), dalpha =
+    sum_k sum(D_k h_k) / rms_k, db = sum_k D_k."""
+    D = np.asarray(D, dtype=np.float64).reshape(-1, 16)
+    h = np.asarray(h, dtype=np.float64).reshape(-1, 16)
+    rms = np.asarray(rms, dtype=np.float64).reshape(-1)
+    alpha = float(alpha)
+    q = (D * h).sum(axis=1)
+    dh = D * (alpha / rms)[:, None]
+    drms = -alpha / rms ** 2 * q
+    dalpha = float((q / rms).sum())
+    db = D.sum(axis=0).reshape(4, 4)
+    return dh, drms, dalpha, db
+
+
+class RefHRes:
+    """The reference's H_res producer (fused_h_activations, src/utils.cuh:50-127)
+    compiled unmodified from its header (``ref_hres_shim.cu``), plus the
+    producer's pre-exponential value restated with the same expression and
+    flags.  Calls take raw device pointers (ints) and a raw stream (int)."""
+
+    def __init__(self, path: str = REF_HRES_LIB):
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is not built; run `make -C oracle ref` where the reference sources exist")
+        lib = ctypes.CDLL(path)
+        vp, f32, i32 = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
+        lib.ref_fused_h_activations_n4.argtypes = [vp, vp, vp, vp, vp, f32, f32, f32, vp, vp, vp, i32, vp]
+        lib.ref_fused_h_activations_n4.restype = ctypes.c_int
+        lib.ref_hres_logits_n4.argtypes = [vp, vp, f32, vp, vp, i32, vp]
+        lib.ref_hres_logits_n4.restype = ctypes.c_int
+        lib.ref_fast_exp.argtypes = [vp, vp, i32, vp]
+        lib.ref_fast_exp.restype = ctypes.c_int
+        self.lib = lib
+
+    @staticmethod
+    def available(path: str = REF_HRES_LIB) -> bool:
+        return os.path.exists(path)
+
+    def fused_h_activations_n4(self, H_pre, H_post, H_res, H_proj_concat, rms, alpha_pre, alpha_post, alpha_res,
+                               b_pre, b_post, b_res, B, stream):
+        rc = self.lib.ref_fused_h_activations_n4(H_pre, H_post, H_res, H_proj_concat, rms, float(alpha_pre),
+                                                 float(alpha_post), float(alpha_res), b_pre, b_post, b_res, int(B),
+                                                 stream)
+        if rc != 0:
+            raise RuntimeError(f"reference fused_h_activations failed with code {rc}")
+
+    def hres_logits_n4(self, H_proj_concat, rms, alpha_res, b_res, R, B, stream):
+        rc = self.lib.ref_hres_logits_n4(H_proj_concat, rms, float(alpha_res), b_res, R, int(B), stream)
+        if rc != 0:
+            raise RuntimeError(f"reference H_res logits failed with code {rc}")
+
+    def fast_exp(self, x, y, n, stream):
+        rc = self.lib.ref_fast_exp(x, y, int(n), stream)
+        if rc != 0:
+            raise RuntimeError(f"reference fast_exp failed with code {rc}")

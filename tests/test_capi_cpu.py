@@ -81,3 +81,31 @@ def test_ex_invalid_arguments_rejected(fn, args):
     with pytest.raises(capi.MhcError) as e:
         fn(*args)
     assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("fn,args", [
+    (capi.birkhoff_proj_n4_hres, (FAKE, 24, FAKE, FAKE, FAKE, FAKE, 1e-6, -1)),
+    (capi.birkhoff_proj_n4_hres, (FAKE, -24, FAKE, FAKE, FAKE, FAKE, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_hres, (FAKE, 24, 0, FAKE, FAKE, FAKE, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_hres, (FAKE, 24, FAKE, 0, FAKE, FAKE, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_hres, (FAKE, 24, FAKE, FAKE, 0, FAKE, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_hres_backward, (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, -1,
+                                           FAKE, 68)),
+    (capi.birkhoff_proj_n4_hres_backward, (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, -16, FAKE, FAKE, FAKE, 5,
+                                           FAKE, 68)),
+    (capi.birkhoff_proj_n4_hres_backward, (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, 0, FAKE, 5,
+                                           FAKE, 68)),
+    (capi.birkhoff_proj_n4_hres_backward, (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, 5,
+                                           0, 68)),
+    (capi.birkhoff_proj_n4_hres_backward, (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, 5,
+                                           FAKE, -4)),
+    (capi.birkhoff_proj_n4_hres_backward_workspace, (-1,)),
+])
+def test_hres_invalid_arguments_rejected(fn, args):
+    with pytest.raises(capi.MhcError) as e:
+        fn(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+
+
+def test_hres_forward_empty_batch_is_a_no_op():
+    capi.birkhoff_proj_n4_hres(0, 24, 0, 0, 0, 0, 1e-6, 0)
