@@ -39,6 +39,8 @@ METRIC = "fwd+bwd matrices/s and % HBM roofline at N=2^24 fp32, 1/2/4/8 B200"
 UNIT = "matrices/s"
 BYTES_FWD = 128      # R in (64 B) + T out (64 B) per matrix
 BYTES_BWD = 192      # G, T in + D out per matrix
+BYTES_HRES_FWD = 132  # h (64 B of a 96 B row) + rms in, T out
+BYTES_HRES_BWD = 264  # G, T, h, rms in; dh, drms out
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -48,9 +50,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["newton", "sinkhorn"], default="newton",
+    ap.add_argument("--workload", choices=["newton", "sinkhorn", "hres"], default="newton",
                     help="newton: the Newton forward + IFT backward (default, the headline metric); "
-                         "sinkhorn: the fused exp + Sinkhorn-Knopp pair, 20 iterations")
+                         "sinkhorn: the fused exp + Sinkhorn-Knopp pair, 20 iterations; "
+                         "hres: the projection fused with the mHC layer's H_res producer, forward + backward")
     ap.add_argument("--n", type=int, default=None, help="matrices per GPU (default 2^24, or 2^22 for sinkhorn)")
     ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
     ap.add_argument("--tol", type=float, default=1e-6)
@@ -99,6 +102,9 @@ def sm_count(dev):
 def workload_config(args, world):
     if args.workload == "sinkhorn":
         what = "fused exp + Sinkhorn-Knopp n4 (20 iterations) forward + backward"
+    elif args.workload == "hres":
+        what = (f"H_res producer (alpha*h/rms+b, h = columns 8..23 of an [N,24] projection) fused with the Newton "
+                f"forward (tol {args.tol:g}) + fused backward incl. dalpha, db batch sums")
     else:
         what = f"Newton forward (tol {args.tol:g}) + IFT backward"
     return {
@@ -287,9 +293,15 @@ def run_ours(args):
     R = make_logits(args.dist, n, seed=1000 + rank, device=dev)
     G = make_logits("normal", n, seed=2000 + rank, device=dev)
     tol = args.tol
+    hres = None
     if args.workload == "sinkhorn":
         fwd = lambda: mhc_proj.torch.sinkhorn_knopp_n4_logits(R, 20)["T"]  # noqa: E731
         bwd = lambda T: mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(G, R, 20)["D"]  # noqa: E731
+    elif args.workload == "hres":
+        hres = hres_inputs(R, rank, dev)
+        h, rms, a, b = hres
+        fwd = lambda: mhc_proj.torch.birkhoff_proj_n4_hres(h, rms, a, b, tol)["T"]  # noqa: E731
+        bwd = lambda T: mhc_proj.torch.birkhoff_proj_n4_hres_backward(G, T, h, rms, a, b_res=b)  # noqa: E731
     else:
         fwd = lambda: mhc_proj.torch.birkhoff_proj_n4(R, tol)["T"]  # noqa: E731
         bwd = lambda T: mhc_proj.torch.birkhoff_proj_n4_backward(G, T)["D"]  # noqa: E731
@@ -332,6 +344,8 @@ def run_ours(args):
     # up, T and D come back, chunks pipelined over two streams
     e2e = run_e2e(args, R, G, dev, world) if args.workload == "newton" else {"ms": float("nan"), "h2d": 0, "d2h": 0, "how": "not measured for this workload"}
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
+    if args.workload == "hres":
+        unfused_ms = hres_unfused_ms(hres, G, tol, args.steps)
 
     stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
     if world > 1:
@@ -403,6 +417,27 @@ def run_ours(args):
                 "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
                 "how": "torch.exp, sinkhorn_knopp_n4, sinkhorn_knopp_n4_backward, product with exp(R) "
                        "(the reference MHCSinkhornN4 composition) on this repository's kernels"}
+        if args.workload == "hres":
+            fwd_gbs = BYTES_HRES_FWD * n / (fwd_ms * 1e-3) / 1e9
+            bwd_gbs = BYTES_HRES_BWD * n / (bwd_ms * 1e-3) / 1e9
+            step_gbs = (BYTES_HRES_FWD + BYTES_HRES_BWD) * n / (ms_per_step * 1e-3) / 1e9
+            line["metric"] = "H_res producer + Newton projection fwd+bwd matrices/s"
+            line["roofline"].update({
+                "kernel": "birkhoff_fwd_kernel<HResSource> (producer fused into the Newton forward)",
+                "achieved": fwd_gbs, "frac": fwd_gbs / peak, "algorithmic_bytes_per_matrix": BYTES_HRES_FWD,
+                "traffic": None,
+                "step": {"achieved": step_gbs, "frac": step_gbs / peak,
+                         "algorithmic_bytes_per_matrix": BYTES_HRES_FWD + BYTES_HRES_BWD},
+                "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms, "forward_gbs": fwd_gbs,
+                            "backward_gbs": bwd_gbs, "backward_frac": bwd_gbs / peak,
+                            "backward_kernels": "birkhoff_hres_bwd_kernel + hres_reduce_kernel"}})
+            line["roofline"]["compute"] = None
+            line["e2e"] = None
+            line["gpu_launches"] = 3 * args.steps
+            line["unfused_composition"] = {
+                "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
+                "how": "R = alpha*h/rms + b with torch ops, birkhoff_proj_n4, birkhoff_proj_n4_backward, then "
+                       "dh, drms, dalpha, db with torch ops (this repository's unfused kernels)"}
         if world == 1 and not args.no_cpu_baseline and args.workload == "newton":
             rate, nt, done = cpu_port_rate(args.cpu_seconds, 1 << 18, args.dist, tol)
             line["cpu_baseline"] = {
@@ -416,6 +451,56 @@ def run_ours(args):
         dist.barrier(device_ids=[dev.index])
         dist.destroy_process_group()
     return 0
+
+
+def hres_inputs(R, rank, dev):
+    """The mHC layer's producer inputs of the hres workload: H_proj_concat
+    [N, 24] with the logits' values in columns 8..23 (the H_res block), rms
+    ~ U(0.5, 2), alpha_res = 1 and b_res ~ N(0,1) + 2 I, seeded per rank."""
+    import torch
+
+    n = R.shape[0]
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    H = torch.randn(n, 24, device=dev, generator=g)
+    H[:, 8:24] = R.reshape(n, 16)
+    rms = torch.rand(n, device=dev, generator=g) * 1.5 + 0.5
+    b = torch.randn(16, device=dev, generator=g) + 2.0 * torch.eye(4, device=dev).reshape(16)
+    a = torch.ones(1, device=dev)
+    return H[:, 8:24], rms, a, b
+
+
+def hres_unfused_ms(hres, G, tol, steps):
+    """Device time of the same step as separate kernels: the producer's
+    arithmetic and the chain rule as torch ops around the plain projection
+    kernels."""
+    import torch
+
+    import mhc_proj
+
+    h, rms, a, b = hres
+    n = h.shape[0]
+
+    def once():
+        R = (a * h / rms[:, None] + b).reshape(n, 4, 4)
+        T = mhc_proj.torch.birkhoff_proj_n4(R, tol)["T"]
+        D = mhc_proj.torch.birkhoff_proj_n4_backward(G, T)["D"].reshape(n, 16)
+        s = a / rms
+        dh = D * s[:, None]
+        q = (D * h).sum(1)
+        drms = -(s / rms) * q
+        return dh, drms, (q / rms).sum(), D.sum(0)
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def sinkhorn_unfused_ms(R, G, steps):

@@ -167,6 +167,24 @@ MHC_API int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float* d_
                                                void* d_workspace, int64_t workspace_bytes,
                                                cudaStream_t stream);
 
+/* mhc_birkhoff_proj_n4_hres_backward without a caller workspace and with no
+ * allocation of any kind: the partial sums go to a fixed 68 KB array in the
+ * library's device memory (1024 rows of 17 floats; the call uses at most
+ * 1024 blocks, so every N fits), whose address is looked up once per device
+ * on the first call there.  Same results as the workspace form given the
+ * size that mhc_birkhoff_proj_n4_hres_backward_workspace reports (on a GPU
+ * whose resident-block wave is at most 1024 blocks, B200 included).  The
+ * array is shared by every call on a device: calls whose kernels may overlap
+ * on the GPU (different streams without ordering) race and must not be
+ * issued.  Nothing in it has to start at zero: each call writes every row it
+ * reads first.  No reference counterpart. */
+MHC_API int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, const float* d_T,
+                                                       const float* d_h, int64_t h_stride,
+                                                       const float* d_rms, const float* d_alpha,
+                                                       float* d_dh, int64_t dh_stride, float* d_drms,
+                                                       float* d_dalpha, float* d_db, int64_t N,
+                                                       cudaStream_t stream);
+
 /* Human-readable text for a return code of the functions above. */
 MHC_API const char* mhc_status_string(int status);
 

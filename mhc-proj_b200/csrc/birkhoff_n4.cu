@@ -471,6 +471,28 @@ static int hres_backward_launch(const float* G, const float* T, const float* h, 
     return static_cast<int>(cudaGetLastError());
 }
 
+// Scratch of mhc_birkhoff_proj_n4_hres_backward_noalloc: partial sums for up
+// to kNoAllocRows blocks (68 KB), in the library's own device memory.  Every
+// call writes each row it reads before reading it, so nothing in it has to
+// start at zero; calls whose kernels overlap on the GPU share it and race.
+constexpr int kNoAllocRows = 1024;
+static __device__ __align__(256) float g_hres_partials[kNoAllocRows * kHResPartials];
+
+// Address of g_hres_partials on the current device, looked up once per device.
+static float* noalloc_partials()
+{
+    static std::atomic<float*> cache[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    float* p = cache[dev].load(std::memory_order_acquire);
+    if (p) return p;
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_hres_partials) != cudaSuccess) return nullptr;
+    p = static_cast<float*>(addr);
+    cache[dev].store(p, std::memory_order_release);
+    return p;
+}
+
 static bool valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
 
 }  // namespace mhcp
@@ -572,6 +594,25 @@ extern "C" int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float*
     if (N > 0 && blocks == 0) return MHC_ERR_INVALID_VALUE;  // workspace smaller than one row
     return hres_backward_launch(d_G, d_T, d_h, h_stride, d_rms, d_alpha, d_dh, dh_stride, d_drms, d_dalpha, d_db, N,
                                 static_cast<float*>(d_workspace), blocks, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, const float* d_T, const float* d_h,
+                                                          int64_t h_stride, const float* d_rms, const float* d_alpha,
+                                                          float* d_dh, int64_t dh_stride, float* d_drms,
+                                                          float* d_dalpha, float* d_db, int64_t N,
+                                                          cudaStream_t stream)
+{
+    if (N < 0 || h_stride < 0 || dh_stride < 0 || !d_dalpha || !d_db ||
+        (N > 0 && (!d_G || !d_T || !d_h || !d_rms || !d_alpha || !d_dh || !d_drms)))
+        return MHC_ERR_INVALID_VALUE;
+    float* partials = noalloc_partials();
+    const int blocks = partials ? hres_backward_blocks(N, kNoAllocRows) : -1;
+    if (blocks < 0) {
+        const cudaError_t e = cudaGetLastError();
+        return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
+    }
+    return hres_backward_launch(d_G, d_T, d_h, h_stride, d_rms, d_alpha, d_dh, dh_stride, d_drms, d_dalpha, d_db, N,
+                                partials, blocks, stream);
 }
 
 extern "C" const char* mhc_status_string(int status)

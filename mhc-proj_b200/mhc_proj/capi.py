@@ -26,6 +26,7 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_hres",
     "mhc_birkhoff_proj_n4_hres_backward_workspace",
     "mhc_birkhoff_proj_n4_hres_backward",
+    "mhc_birkhoff_proj_n4_hres_backward_noalloc",
     "mhc_status_string",
     "mhc_abi_version",
 )
@@ -67,6 +68,8 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_hres_backward_workspace.argtypes = [i64, ctypes.POINTER(i64)]
         L.mhc_birkhoff_proj_n4_hres_backward.argtypes = [vp, vp, vp, i64, vp, vp, vp, i64, vp, vp, vp, i64, vp,
                                                          i64, vp]
+        L.mhc_birkhoff_proj_n4_hres_backward_noalloc.argtypes = [vp, vp, vp, i64, vp, vp, vp, i64, vp, vp, vp,
+                                                                 i64, vp]
         for f in _LAUNCHERS:
             getattr(L, f).restype = ctypes.c_int
         L.mhc_status_string.argtypes = [ctypes.c_int]
@@ -149,6 +152,16 @@ def birkhoff_proj_n4_hres_backward(G: int, T: int, h: int, h_stride: int, rms: i
     _check(lib().mhc_birkhoff_proj_n4_hres_backward(G, T, h, h_stride, rms, alpha, dh, dh_stride, drms, dalpha, db,
                                                      N, workspace, workspace_bytes, stream),
            "mhc_birkhoff_proj_n4_hres_backward")
+
+
+def birkhoff_proj_n4_hres_backward_noalloc(G: int, T: int, h: int, h_stride: int, rms: int, alpha: int, dh: int,
+                                           dh_stride: int, drms: int, dalpha: int, db: int, N: int,
+                                           stream: int = 0) -> None:
+    """The backward with the library's fixed device scratch instead of a
+    workspace; calls that may overlap on the GPU race (see the header)."""
+    _check(lib().mhc_birkhoff_proj_n4_hres_backward_noalloc(G, T, h, h_stride, rms, alpha, dh, dh_stride, drms,
+                                                             dalpha, db, N, stream),
+           "mhc_birkhoff_proj_n4_hres_backward_noalloc")
 
 
 # --- tensor conveniences ---------------------------------------------------

@@ -109,3 +109,15 @@ def test_hres_invalid_arguments_rejected(fn, args):
 
 def test_hres_forward_empty_batch_is_a_no_op():
     capi.birkhoff_proj_n4_hres(0, 24, 0, 0, 0, 0, 1e-6, 0)
+
+
+@pytest.mark.parametrize("args", [
+    (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, -1),
+    (FAKE, FAKE, FAKE, -24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, 5),
+    (FAKE, FAKE, FAKE, 24, FAKE, FAKE, FAKE, 16, FAKE, 0, FAKE, 5),
+    (FAKE, FAKE, 0, 24, FAKE, FAKE, FAKE, 16, FAKE, FAKE, FAKE, 5),
+])
+def test_hres_noalloc_invalid_arguments_rejected(args):
+    with pytest.raises(capi.MhcError) as e:
+        capi.birkhoff_proj_n4_hres_backward_noalloc(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE

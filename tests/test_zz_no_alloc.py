@@ -1,0 +1,82 @@
+"""The no-allocation form of the fused H_res backward
+(mhc_birkhoff_proj_n4_hres_backward_noalloc), which keeps its partial sums in
+a fixed array of the library's device memory instead of a caller workspace.
+
+Collected last on purpose (the file name), so that it runs both after every
+other GPU test and on its own: two calls in a row, on different batches and
+sizes, each give the bits of the workspace entry point on the same inputs --
+the fixed array needs no reset between calls."""
+import pytest
+import torch
+
+from mhc_proj import capi
+
+pytestmark = pytest.mark.gpu
+
+
+def inputs(n, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    H = torch.randn(n, 24, device="cuda", generator=g)
+    rms = torch.rand(n, device="cuda", generator=g) * 1.5 + 0.5
+    a = torch.tensor([0.9], device="cuda")
+    b = torch.randn(16, device="cuda", generator=g) + 2.0 * torch.eye(4, device="cuda").reshape(16)
+    G = torch.randn(n, 4, 4, device="cuda", generator=g)
+    h = H[:, 8:24]
+    T = capi.birkhoff_proj_n4_hres_tensor(h, rms, a, b)
+    return G, T, h, rms, a
+
+
+def outputs(n):
+    return (torch.empty(n, 16, device="cuda"), torch.empty(n, device="cuda"), torch.empty((), device="cuda"),
+            torch.empty(4, 4, device="cuda"))
+
+
+def with_workspace(G, T, h, rms, a):
+    n = h.shape[0]
+    dh, drms, dalpha, db = outputs(n)
+    nbytes = capi.birkhoff_proj_n4_hres_backward_workspace(n)
+    ws = torch.empty(nbytes // 4, device="cuda")
+    capi.birkhoff_proj_n4_hres_backward(G.data_ptr(), T.data_ptr(), h.data_ptr(), h.stride(0), rms.data_ptr(),
+                                        a.data_ptr(), dh.data_ptr(), 16, drms.data_ptr(), dalpha.data_ptr(),
+                                        db.data_ptr(), n, ws.data_ptr(), nbytes,
+                                        torch.cuda.current_stream().cuda_stream)
+    return dh, drms, dalpha, db
+
+
+def without_allocation(G, T, h, rms, a):
+    n = h.shape[0]
+    dh, drms, dalpha, db = outputs(n)
+    capi.birkhoff_proj_n4_hres_backward_noalloc(G.data_ptr(), T.data_ptr(), h.data_ptr(), h.stride(0),
+                                                rms.data_ptr(), a.data_ptr(), dh.data_ptr(), 16, drms.data_ptr(),
+                                                dalpha.data_ptr(), db.data_ptr(), n,
+                                                torch.cuda.current_stream().cuda_stream)
+    return dh, drms, dalpha, db
+
+
+def same_bits(x, y):
+    return torch.equal(x.contiguous().view(torch.int32), y.contiguous().view(torch.int32))
+
+
+def test_two_calls_in_a_row_match_the_workspace_entry_point():
+    first = inputs(1 << 20, 1)
+    second = inputs(77777, 2)
+    got1 = without_allocation(*first)
+    got2 = without_allocation(*second)  # reuses the same scratch right after the first call
+    want1 = with_workspace(*first)
+    want2 = with_workspace(*second)
+    torch.cuda.synchronize()
+    for g, w in zip(got1, want1):
+        assert same_bits(g, w)
+    for g, w in zip(got2, want2):
+        assert same_bits(g, w)
+
+
+def test_empty_batch_writes_zero_sums():
+    G, T, h, rms, a = inputs(0, 3)
+    dh, drms, dalpha, db = outputs(0)
+    dalpha.fill_(5.0)
+    db.fill_(5.0)
+    capi.birkhoff_proj_n4_hres_backward_noalloc(0, 0, 0, 24, 0, a.data_ptr(), 0, 16, 0, dalpha.data_ptr(),
+                                                db.data_ptr(), 0, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert float(dalpha) == 0.0 and bool((db == 0).all())
