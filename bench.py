@@ -345,7 +345,7 @@ def run_ours(args):
     e2e = run_e2e(args, R, G, dev, world) if args.workload == "newton" else {"ms": float("nan"), "h2d": 0, "d2h": 0, "how": "not measured for this workload"}
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
     if args.workload == "hres":
-        unfused_ms = hres_unfused_ms(hres, G, tol, args.steps)
+        unfused_ms, plain_fwd_ms = hres_unfused_ms(hres, G, tol, args.steps)
 
     stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
     if world > 1:
@@ -437,7 +437,9 @@ def run_ours(args):
             line["unfused_composition"] = {
                 "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
                 "how": "R = alpha*h/rms + b with torch ops, birkhoff_proj_n4, birkhoff_proj_n4_backward, then "
-                       "dh, drms, dalpha, db with torch ops (this repository's unfused kernels)"}
+                       "dh, drms, dalpha, db with torch ops (this repository's unfused kernels)",
+                "plain_forward_ms": plain_fwd_ms,
+                "plain_forward_how": "birkhoff_proj_n4 alone on the same logits materialised in HBM"}
         if world == 1 and not args.no_cpu_baseline and args.workload == "newton":
             rate, nt, done = cpu_port_rate(args.cpu_seconds, 1 << 18, args.dist, tol)
             line["cpu_baseline"] = {
@@ -490,17 +492,22 @@ def hres_unfused_ms(hres, G, tol, steps):
         drms = -(s / rms) * q
         return dh, drms, (q / rms).sum(), D.sum(0)
 
-    for _ in range(3):
-        once()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        once()
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / steps
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    R = (a * h / rms[:, None] + b).reshape(n, 4, 4)
+    plain_fwd = timed(lambda: mhc_proj.torch.birkhoff_proj_n4(R, tol))
+    return timed(once), plain_fwd
 
 
 def sinkhorn_unfused_ms(R, G, steps):

@@ -7,6 +7,10 @@
 namespace mhcp {
 
 constexpr int kNewtonBlock = 128;
+// Each forward warp stages its next matrices in a shared-memory ring of
+// kRing slots, kRingHalf at a time (8 KB per warp, 32 KB per block).
+constexpr int kRingHalf = 64;
+constexpr int kRing = 2 * kRingHalf;
 constexpr int kBackwardBlock = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -84,13 +88,22 @@ struct HResSource {
 // writes its T as well, for the one exit that comes after a column pass (the
 // alpha = 0 initialisation rejected and beta = 0 already converged).
 //
+// The warp's next matrices wait in a shared-memory ring: all 32 lanes load
+// (and, for HResSource, transform) kRingHalf matrices at once whenever the
+// older half of the ring has been handed out, so that a refill -- which a
+// few lanes of the warp take each step -- is four shared-memory loads
+// instead of global loads and arithmetic issued for those few lanes alone.
+// The bound of 5 blocks per SM keeps the register count at the 5-block
+// occupancy (96 registers) that the ring's addressing would otherwise push
+// past.
+//
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
 // kStats: also write, per matrix, the number of Newton iterations taken and
 // the final gradient l1 norm (a separate instantiation; the plain one carries
 // no cost for it).
 template <class Rd, class Src, class Elem, bool kVec, bool kStats = false>
-__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
+__global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_warp,
                                                                     int32_t* __restrict__ iters_out = nullptr,
                                                                     float* __restrict__ gnorm_out = nullptr)
@@ -122,8 +135,39 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(Src src, Ele
     bool fresh = false;     // a new Newton iteration starts: take the direction now
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
+    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4];
+    float4* ring = ring_all[threadIdx.x >> 5];
+    auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
+#pragma unroll
+        for (int u = 0; u < kRingHalf / 32; ++u) {
+            const int i = first + 32 * u + lane;
+            if (i < cnt) {
+                Mat4 m;
+                src.load(i, m);
+                float4* slot = ring + (i & (kRing - 1)) * 4;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    slot[j] = make_float4(m.m[4 * j], m.m[4 * j + 1], m.m[4 * j + 2], m.m[4 * j + 3]);
+            }
+        }
+    };
+    auto take = [&](int i) {
+        const float4* slot = ring + (i & (kRing - 1)) * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 v = slot[j];
+            r.m[4 * j] = v.x;
+            r.m[4 * j + 1] = v.y;
+            r.m[4 * j + 2] = v.z;
+            r.m[4 * j + 3] = v.w;
+        }
+    };
+    fill(0);
+    fill(kRingHalf);
+    __syncwarp();
+    int base = 0;  // the ring holds matrices [base, base + kRing)
     if (idx < cnt) {
-        src.load(idx, r);
+        take(idx);
         stage = kEval0;
     } else {
 #pragma unroll
@@ -236,11 +280,17 @@ __global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_kernel(Src src, Ele
             if (done) {
                 idx = next + __popc(want & ((1u << lane) - 1u));
                 if (idx < cnt) {
-                    src.load(idx, r);
+                    take(idx);
                     stage = kEval0;
                 }
             }
             next = min(cnt, next + __popc(want));
+            if (next > base + kRingHalf) {  // the older half is all handed out: stage the next one
+                __syncwarp();
+                fill(base + kRing);
+                __syncwarp();
+                base += kRingHalf;
+            }
         }
     }
 }
