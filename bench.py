@@ -348,7 +348,10 @@ def run_ours(args):
         unfused_ms, plain_fwd_ms = hres_unfused_ms(hres, G, tol, args.steps)
 
     stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
+    per_rank = [stats.clone()]
     if world > 1:
+        per_rank = [torch.empty_like(stats) for _ in range(world)]
+        dist.all_gather(per_rank, stats)
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     total_ms, fwd_ms, bwd_ms, e2e_ms = stats.tolist()
     ms_per_step = total_ms / args.steps
@@ -407,6 +410,8 @@ def run_ours(args):
                     "ms_per_step": e2e_ms, "how": e2e["how"]},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
+            "per_rank": [{"rank": i, "ms_per_step": t[0] / args.steps, "forward_ms": t[1], "backward_ms": t[2]}
+                         for i, t in enumerate(x.tolist() for x in per_rank)],
         }
         if args.workload == "sinkhorn":
             line["metric"] = "Sinkhorn-Knopp n4 (20 iterations) fwd+bwd matrices/s"
