@@ -185,6 +185,34 @@ MHC_API int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, const f
                                                        float* d_dalpha, float* d_db, int64_t N,
                                                        cudaStream_t stream);
 
+/* Sinkhorn-Knopp on the mHC layer's H_res activation: M[k] = exp(alpha *
+ * h[k] / rms[k] + b) formed in the kernel's load exactly as the reference's
+ * producer forms it (fused_h_activations, src/utils.cuh:84-93, with its
+ * __expf, utils.cuh:42-44), then the normalisations of mhc_sinkhorn_knopp_n4.
+ * h, h_stride, rms, alpha and b as for mhc_birkhoff_proj_n4_hres.  T is the
+ * same as the reference's producer followed by its sinkhorn_knopp_n4.  No
+ * reference counterpart: there the producer writes H_res to memory. */
+MHC_API int mhc_sinkhorn_knopp_n4_hres(const float* d_h, int64_t h_stride, const float* d_rms,
+                                       const float* d_alpha, const float* d_b, float* d_T, int64_t N,
+                                       int num_iters, cudaStream_t stream);
+
+/* Bytes of device workspace that mhc_sinkhorn_knopp_n4_hres_backward needs for
+ * N matrices (68 per block of 128 matrices). */
+MHC_API int mhc_sinkhorn_knopp_n4_hres_backward_workspace(int64_t N, int64_t* bytes);
+
+/* Backward of mhc_sinkhorn_knopp_n4_hres given G = dL/dT: with dM the exact
+ * gradient with respect to M (mhc_sinkhorn_knopp_n4_backward) and dR = dM .* M,
+ * the outputs of mhc_birkhoff_proj_n4_hres_backward (dh, drms per matrix;
+ * dalpha and db as deterministic batch sums, overwritten).  The workspace must
+ * hold at least the reported bytes; num_iters > MHC_SK_BACKWARD_MAX_ITERS
+ * returns MHC_ERR_ITERS.  No reference counterpart. */
+MHC_API int mhc_sinkhorn_knopp_n4_hres_backward(const float* d_G, const float* d_h, int64_t h_stride,
+                                                const float* d_rms, const float* d_alpha,
+                                                const float* d_b, float* d_dh, int64_t dh_stride,
+                                                float* d_drms, float* d_dalpha, float* d_db, int64_t N,
+                                                int num_iters, void* d_workspace,
+                                                int64_t workspace_bytes, cudaStream_t stream);
+
 /* Human-readable text for a return code of the functions above. */
 MHC_API const char* mhc_status_string(int status);
 

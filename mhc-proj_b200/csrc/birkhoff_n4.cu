@@ -2,6 +2,7 @@
 #include <atomic>
 
 #include "birkhoff_n4.cuh"
+#include "partial_sums.cuh"
 #include "mhc_proj.h"
 
 namespace mhcp {
@@ -61,10 +62,10 @@ struct HResSource {
     __device__ __forceinline__ void load(int i, Mat4& r) const
     {
         load_elems<float, kVec>(h, static_cast<int64_t>(i) * stride, r);
-        const float rinv = fast_rcp(__ldg(rms + i));
+        const float rinv = hres_rinv(__ldg(rms + i));
         const float a = __ldg(alpha);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) r.m[e] = __fmaf_rn(__fmul_rn(a, r.m[e]), rinv, __ldg(b + e));
+        for (int e = 0; e < 16; ++e) r.m[e] = hres_logit(a, r.m[e], rinv, __ldg(b + e));
     }
 };
 
@@ -315,14 +316,13 @@ __global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const GE* 
 // The H_res backward: the IFT gradient D = dL/dR of each matrix, carried
 // through R = alpha * h / rms + b.  Per matrix, dh = D * (alpha / rms) and
 // drms = -(alpha / rms^2) * sum(D .* h); over the batch, dalpha =
-// sum_k sum(D_k .* h_k) / rms_k and db = sum_k D_k.  The two batch sums are
-// reduced deterministically: each thread accumulates a fixed set of
-// matrices (grid-stride order), each block folds its threads in a fixed
-// tree into kHResPartials floats of `partials`, and hres_reduce_kernel folds
-// the blocks in a fixed order.  The same N on the same GPU model therefore
-// always gives the same bits.
+// sum_k sum(D_k .* h_k) / rms_k and db = sum_k D_k.  The batch sums are
+// deterministic (partial_sums.cuh): each thread accumulates a fixed set of
+// matrices (grid-stride order), each block folds its threads in a fixed tree
+// into one row of `partials`, and partial_sums_fold_kernel folds the rows in
+// a fixed order.  The same N on the same GPU model therefore always gives the
+// same bits.
 constexpr int kHResBlock = 256;
-constexpr int kHResPartials = 17;  // db[0..15], dalpha
 
 template <bool kVec>
 __global__ void __launch_bounds__(kHResBlock) birkhoff_hres_bwd_kernel(
@@ -336,67 +336,15 @@ __global__ void __launch_bounds__(kHResBlock) birkhoff_hres_bwd_kernel(
     const float a = __ldg(alpha);
     const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < N; idx += step) {
-        Mat4 g, t, d, x;
+        Mat4 g, t, d, x, dx;
         load_elems<float, kVec>(G, idx * 16, g);
         load_elems<float, kVec>(T, idx * 16, t);
         ift_backward<RefRounding>(g, t, d);
         load_elems<float, kVec>(h, idx * h_stride, x);
-        const float rinv = fast_rcp(__ldg(rms + idx));
-        const float s = __fmul_rn(a, rinv);
-        float rows[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int o = 4 * i;
-            rows[i] = __fmaf_rn(d.m[o + 3], x.m[o + 3],
-                      __fmaf_rn(d.m[o + 2], x.m[o + 2], __fmaf_rn(d.m[o + 1], x.m[o + 1], __fmul_rn(d.m[o], x.m[o]))));
-        }
-        const float q = psum4(rows[0], rows[1], rows[2], rows[3]);
-        drms[idx] = -__fmul_rn(__fmul_rn(s, rinv), q);
-        acc[16] = __fmaf_rn(rinv, q, acc[16]);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            acc[e] = __fadd_rn(acc[e], d.m[e]);
-            x.m[e] = __fmul_rn(d.m[e], s);
-        }
-        store_elems<float, kVec>(dh, idx * dh_stride, x);
+        drms[idx] = hres_chain(d, x, a, hres_rinv(__ldg(rms + idx)), dx, acc);
+        store_elems<float, kVec>(dh, idx * dh_stride, dx);
     }
-    // Fold the block: butterflies within each warp, then warp 0 over warps.
-    __shared__ float part[kHResBlock / 32][kHResPartials];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int q = 0; q < kHResPartials; ++q) {
-        float v = acc[q];
-#pragma unroll
-        for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFullMask, v, m));
-        if (lane == 0) part[warp][q] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < kHResPartials) {
-        float v = part[0][threadIdx.x];
-#pragma unroll
-        for (int w = 1; w < kHResBlock / 32; ++w) v = __fadd_rn(v, part[w][threadIdx.x]);
-        partials[static_cast<int64_t>(blockIdx.x) * kHResPartials + threadIdx.x] = v;
-    }
-}
-
-// Folds `blocks` rows of kHResPartials partial sums into db[16] and dalpha:
-// warp q takes column q, its lanes stride over the rows, then a butterfly.
-// blocks == 0 writes zeros (the gradient of an empty batch).
-__global__ void __launch_bounds__(32 * kHResPartials) hres_reduce_kernel(const float* __restrict__ partials,
-                                                                            int blocks, float* __restrict__ db,
-                                                                            float* __restrict__ dalpha)
-{
-    const int lane = threadIdx.x & 31, q = threadIdx.x >> 5;
-    float v = 0.0f;
-    for (int b = lane; b < blocks; b += 32) v = __fadd_rn(v, partials[static_cast<int64_t>(b) * kHResPartials + q]);
-#pragma unroll
-    for (int m = 16; m > 0; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFullMask, v, m));
-    if (lane == 0) {
-        if (q < 16)
-            db[q] = v;
-        else
-            *dalpha = v;
-    }
+    block_partial_sums<kHResBlock>(acc, partials, gridDim.x, blockIdx.x);
 }
 
 // Resident warps of a forward kernel instantiation on the current device,
@@ -517,7 +465,7 @@ static int hres_backward_launch(const float* G, const float* T, const float* h, 
             birkhoff_hres_bwd_kernel<false><<<blocks, kHResBlock, 0, stream>>>(G, T, h, h_stride, rms, alpha, dh,
                                                                                dh_stride, drms, partials, N);
     }
-    hres_reduce_kernel<<<1, 32 * kHResPartials, 0, stream>>>(partials, blocks, db, dalpha);
+    partial_sums_fold_kernel<kHResPartials><<<1, 32 * kHResPartials, 0, stream>>>(partials, blocks, db, dalpha);
     return static_cast<int>(cudaGetLastError());
 }
 

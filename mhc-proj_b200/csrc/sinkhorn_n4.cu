@@ -7,9 +7,11 @@
 // correctly rounded reciprocal, which that flag does not change, and expf in
 // the fused kernels is then the accurate one, the same function PyTorch's
 // exp kernel calls, so fused and unfused paths agree.
+#include <type_traits>
 #include <utility>
 
 #include "sinkhorn_n4.cuh"
+#include "partial_sums.cuh"
 #include "mhc_proj.h"
 
 namespace mhcp {
@@ -24,42 +26,79 @@ __device__ __forceinline__ void exp_inplace(Mat4& x)
     for (int e = 0; e < 16; ++e) x.m[e] = expf(x.m[e]);
 }
 
-// kLogits: the input is R and the kernel forms M = exp(R) itself.
-template <bool kVec, bool kLogits>
-__global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(const float* __restrict__ M, float* __restrict__ T,
-                                                          int64_t N, int iters)
+// Where the kernels find M, matrix idx of the batch:
+//   MInput     M itself (row-major, contiguous);
+//   ExpInput   the logits R, M = exp(R) with the accurate expf (as torch.exp);
+//   HResInput  the mHC layer's H_res block, M = exp of the producer's
+//              pre-activation alpha * h / rms + b with the producer's own
+//              __expf (src/utils.cuh:42-44,84-93), i.e. its H_res output.
+struct MInput {
+    const float* M;
+    template <bool kVec>
+    __device__ __forceinline__ void load(int64_t idx, Mat4& x) const { load_mat<kVec>(M, idx, x); }
+};
+
+struct ExpInput {
+    const float* R;
+    template <bool kVec>
+    __device__ __forceinline__ void load(int64_t idx, Mat4& x) const
+    {
+        load_mat<kVec>(R, idx, x);
+        exp_inplace(x);
+    }
+};
+
+struct HResInput {
+    const float* h;
+    int64_t stride;
+    const float* rms;
+    const float* alpha;
+    const float* b;
+    // h[idx] and 1 / rms[idx] (the backward needs both again).
+    template <bool kVec>
+    __device__ __forceinline__ float load_h(int64_t idx, Mat4& x) const
+    {
+        load_elems<float, kVec>(h, idx * stride, x);
+        return hres_rinv(__ldg(rms + idx));
+    }
+    __device__ __forceinline__ void activate(const Mat4& hx, float rinv, Mat4& m) const
+    {
+        const float a = __ldg(alpha);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) m.m[e] = __expf(hres_logit(a, hx.m[e], rinv, __ldg(b + e)));
+    }
+    template <bool kVec>
+    __device__ __forceinline__ void load(int64_t idx, Mat4& x) const
+    {
+        Mat4 hx;
+        const float rinv = load_h<kVec>(idx, hx);
+        activate(hx, rinv, x);
+    }
+};
+
+template <bool kVec, class In>
+__global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restrict__ T, int64_t N, int iters)
 {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
     Mat4 x0;
-    load_mat<kVec>(M, idx, x0);
-    if constexpr (kLogits) exp_inplace(x0);
+    in.template load<kVec>(idx, x0);
     Pairs x = to_pairs(x0);
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
     store_mat<kVec>(T, idx, from_pairs(x));
 }
 
-// Backward with a compile-time iteration count.  Segment starts are kept in
-// shared memory, [segment][element][thread] so that a warp's accesses fall in
-// distinct banks; each segment is then replayed in registers and reversed.
-// kLogits: the input is R; M = exp(R) is formed here and the result is the
-// gradient with respect to R, dL/dM * M.
-template <int kIters, bool kVec, bool kLogits>
-__global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restrict__ G,
-                                                          const float* __restrict__ M,
-                                                          float* __restrict__ D, int64_t N)
+// The vector-Jacobian product of kIters Sinkhorn-Knopp iterations at x, in
+// two halves so that the caller loads the incoming gradient only after the
+// first: sk_checkpoint runs the forward and keeps each segment's start in
+// shared memory, [segment][element][thread] so that a warp's accesses fall
+// in distinct banks; sk_reverse replays each segment in registers and
+// reverses it into dy.
+template <int kIters>
+__device__ __forceinline__ void sk_checkpoint(Pairs x, float2 (*ckpt)[8][kSkBlock], int tid)
 {
     constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-    __shared__ float2 ckpt[kNumSeg > 0 ? kNumSeg : 1][8][kSkBlock];
-    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (idx >= N) return;
-    const int tid = threadIdx.x;
-
-    Mat4 x0;
-    load_mat<kVec>(M, idx, x0);
-    if constexpr (kLogits) exp_inplace(x0);
-    Pairs x = to_pairs(x0);
 #pragma unroll
     for (int s = 0; s < kNumSeg; ++s) {
 #pragma unroll
@@ -69,15 +108,16 @@ __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restric
             for (int k = 0; k < kSkSeg; ++k) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
         }
     }
+}
 
-    Mat4 g0;
-    load_mat<kVec>(G, idx, g0);
-    Pairs dy = to_pairs(g0);
+template <int kIters>
+__device__ __forceinline__ void sk_reverse(Pairs& dy, float2 (*ckpt)[8][kSkBlock], int tid)
+{
+    constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
 #pragma unroll
     for (int s = kNumSeg - 1; s >= 0; --s) {
-        constexpr int kFull = kSkSeg;
-        const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kFull;
-        Pairs xr[kSkSeg];
+        const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kSkSeg;
+        Pairs x, xr[kSkSeg];
         float ri[kSkSeg][4], ci[kSkSeg][4];
 #pragma unroll
         for (int q = 0; q < 8; ++q) x.p[q] = ckpt[s][q][tid];
@@ -88,15 +128,79 @@ __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restric
         for (int k = kSkSeg - 1; k >= 0; --k)
             if (k < len) sk_iteration_vjp(dy, xr[k], ri[k], ci[k]);
     }
+}
+
+// Checkpoint segments of a kIters backward (at least one array row).
+template <int kIters>
+constexpr int kSkSegments = (kIters + kSkSeg - 1) / kSkSeg > 0 ? (kIters + kSkSeg - 1) / kSkSeg : 1;
+
+// Backward with a compile-time iteration count: D = dL/dM, or with
+// kLogits (ExpInput) the gradient with respect to R, dL/dM * exp(R).
+template <int kIters, bool kVec, bool kLogits>
+__global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restrict__ G,
+                                                          const float* __restrict__ M,
+                                                          float* __restrict__ D, int64_t N)
+{
+    __shared__ float2 ckpt[kSkSegments<kIters>][8][kSkBlock];
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= N) return;
+    {
+        Mat4 x0;
+        if constexpr (kLogits)
+            ExpInput{M}.load<kVec>(idx, x0);
+        else
+            MInput{M}.load<kVec>(idx, x0);
+        sk_checkpoint<kIters>(to_pairs(x0), ckpt, threadIdx.x);
+    }
+    Mat4 g0;
+    load_mat<kVec>(G, idx, g0);
+    Pairs dy = to_pairs(g0);
+    sk_reverse<kIters>(dy, ckpt, threadIdx.x);
     if constexpr (kLogits) {
         Mat4 m;
-        load_mat<kVec>(M, idx, m);
-        exp_inplace(m);
+        ExpInput{M}.load<kVec>(idx, m);
         const Pairs mp = to_pairs(m);
 #pragma unroll
         for (int q = 0; q < 8; ++q) dy.p[q] = __fmul2_rn(dy.p[q], mp.p[q]);
     }
     store_mat<kVec>(D, idx, from_pairs(dy));
+}
+
+// Backward of the producer fused with Sinkhorn-Knopp: dM as above, dR = dM *
+// M, then the producer's chain rule (partial_sums.cuh: dh, drms per matrix;
+// the per-block partial sums of db and dalpha in column blockIdx.x of
+// `partials`).  One matrix per thread; every thread reaches the block fold.
+template <int kIters, bool kVec>
+__global__ void __launch_bounds__(kSkBlock) sk_hres_bwd_kernel(const float* __restrict__ G, HResInput in,
+                                                               float* __restrict__ dh, int64_t dh_stride,
+                                                               float* __restrict__ drms,
+                                                               float* __restrict__ partials, int64_t N)
+{
+    __shared__ float2 ckpt[kSkSegments<kIters>][8][kSkBlock];
+    float acc[kHResPartials];
+#pragma unroll
+    for (int q = 0; q < kHResPartials; ++q) acc[q] = 0.0f;
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx < N) {
+        {
+            Mat4 x0;
+            in.load<kVec>(idx, x0);
+            sk_checkpoint<kIters>(to_pairs(x0), ckpt, threadIdx.x);
+        }
+        Mat4 g0;
+        load_mat<kVec>(G, idx, g0);
+        Pairs dy = to_pairs(g0);
+        sk_reverse<kIters>(dy, ckpt, threadIdx.x);
+        Mat4 hx, m, dR, dx;
+        const float rinv = in.load_h<kVec>(idx, hx);
+        in.activate(hx, rinv, m);
+        const Mat4 dM = from_pairs(dy);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) dR.m[e] = __fmul_rn(dM.m[e], m.m[e]);
+        drms[idx] = hres_chain(dR, hx, __ldg(in.alpha), rinv, dx, acc);
+        store_elems<float, kVec>(dh, idx * dh_stride, dx);
+    }
+    block_partial_sums<kSkBlock>(acc, partials, gridDim.x, blockIdx.x);
 }
 
 template <int kIters, bool kLogits>
@@ -124,10 +228,11 @@ static int sk_forward(const float* d_M, float* d_T, int64_t N, int num_iters, cu
     if (N == 0) return MHC_OK;
     const int iters = num_iters > 0 ? num_iters : 0;
     const int64_t grid = ceil_div(N, kSkBlock);
+    using In = std::conditional_t<kLogits, ExpInput, MInput>;
     if (aligned16(d_M) && aligned16(d_T))
-        sk_fwd_kernel<true, kLogits><<<grid, kSkBlock, 0, stream>>>(d_M, d_T, N, iters);
+        sk_fwd_kernel<true, In><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
     else
-        sk_fwd_kernel<false, kLogits><<<grid, kSkBlock, 0, stream>>>(d_M, d_T, N, iters);
+        sk_fwd_kernel<false, In><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -142,6 +247,25 @@ static int sk_backward(const float* d_G, const float* d_M, float* d_D, int64_t N
     dispatch_sk_bwd<kLogits>(num_iters > 0 ? num_iters : 0, vec, d_G, d_M, d_D, N, stream,
                              std::make_integer_sequence<int, MHC_SK_BACKWARD_MAX_ITERS + 1>{});
     return static_cast<int>(cudaGetLastError());
+}
+
+template <int kIters>
+static void launch_sk_hres_bwd(bool vec, const float* G, const HResInput& in, float* dh, int64_t dh_stride,
+                               float* drms, float* partials, int64_t grid, int64_t N, cudaStream_t stream)
+{
+    if (vec)
+        sk_hres_bwd_kernel<kIters, true><<<grid, kSkBlock, 0, stream>>>(G, in, dh, dh_stride, drms, partials, N);
+    else
+        sk_hres_bwd_kernel<kIters, false><<<grid, kSkBlock, 0, stream>>>(G, in, dh, dh_stride, drms, partials, N);
+}
+
+template <int... Is>
+static void dispatch_sk_hres_bwd(int iters, bool vec, const float* G, const HResInput& in, float* dh,
+                                 int64_t dh_stride, float* drms, float* partials, int64_t grid, int64_t N,
+                                 cudaStream_t stream, std::integer_sequence<int, Is...>)
+{
+    ((iters == Is ? launch_sk_hres_bwd<Is>(vec, G, in, dh, dh_stride, drms, partials, grid, N, stream) : void()),
+     ...);
 }
 
 }  // namespace mhcp
@@ -169,4 +293,51 @@ extern "C" int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const flo
                                                      int num_iters, cudaStream_t stream)
 {
     return sk_backward<true>(d_G, d_R, d_D, N, num_iters, stream);
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_hres(const float* d_h, int64_t h_stride, const float* d_rms,
+                                         const float* d_alpha, const float* d_b, float* d_T, int64_t N,
+                                         int num_iters, cudaStream_t stream)
+{
+    if (N < 0 || h_stride < 0 || (N > 0 && (!d_h || !d_rms || !d_alpha || !d_b || !d_T)))
+        return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    const int iters = num_iters > 0 ? num_iters : 0;
+    const int64_t grid = ceil_div(N, kSkBlock);
+    const HResInput in{d_h, h_stride, d_rms, d_alpha, d_b};
+    if (aligned16(d_h, h_stride, 4) && aligned16(d_T))
+        sk_fwd_kernel<true, HResInput><<<grid, kSkBlock, 0, stream>>>(in, d_T, N, iters);
+    else
+        sk_fwd_kernel<false, HResInput><<<grid, kSkBlock, 0, stream>>>(in, d_T, N, iters);
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_hres_backward_workspace(int64_t N, int64_t* bytes)
+{
+    if (N < 0 || !bytes) return MHC_ERR_INVALID_VALUE;
+    *bytes = max(ceil_div(N, kSkBlock), int64_t{1}) * kHResPartials * static_cast<int64_t>(sizeof(float));
+    return MHC_OK;
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_hres_backward(const float* d_G, const float* d_h, int64_t h_stride,
+                                                  const float* d_rms, const float* d_alpha, const float* d_b,
+                                                  float* d_dh, int64_t dh_stride, float* d_drms, float* d_dalpha,
+                                                  float* d_db, int64_t N, int num_iters, void* d_workspace,
+                                                  int64_t workspace_bytes, cudaStream_t stream)
+{
+    if (N < 0 || h_stride < 0 || dh_stride < 0 || !d_dalpha || !d_db ||
+        (N > 0 && (!d_G || !d_h || !d_rms || !d_alpha || !d_b || !d_dh || !d_drms || !d_workspace)))
+        return MHC_ERR_INVALID_VALUE;
+    if (num_iters > MHC_SK_BACKWARD_MAX_ITERS) return MHC_ERR_ITERS;
+    const int64_t grid = ceil_div(N, kSkBlock);
+    if (workspace_bytes < grid * kHResPartials * static_cast<int64_t>(sizeof(float))) return MHC_ERR_INVALID_VALUE;
+    float* partials = static_cast<float*>(d_workspace);
+    if (N > 0) {
+        const HResInput in{d_h, h_stride, d_rms, d_alpha, d_b};
+        const bool vec = aligned16(d_G) && aligned16(d_h, h_stride, 4) && aligned16(d_dh, dh_stride, 4);
+        dispatch_sk_hres_bwd(num_iters > 0 ? num_iters : 0, vec, d_G, in, d_dh, dh_stride, d_drms, partials, grid, N,
+                             stream, std::make_integer_sequence<int, MHC_SK_BACKWARD_MAX_ITERS + 1>{});
+    }
+    partial_sums_fold_kernel<kHResPartials><<<1, 32 * kHResPartials, 0, stream>>>(partials, grid, d_db, d_dalpha);
+    return static_cast<int>(cudaGetLastError());
 }

@@ -13,8 +13,8 @@
 //   - extra keyword arguments are accepted and ignored.
 // Functions with no reference counterpart: sinkhorn_knopp_n4_logits and its
 // backward take the logits R and fuse exp(R) (and, backward, the product with
-// exp(R)) into the kernels; birkhoff_proj_n4_hres and its backward fuse the
-// mHC layer's H_res pre-activation into the projection.
+// exp(R)) into the kernels; birkhoff_proj_n4_hres, sinkhorn_knopp_n4_hres and
+// their backwards fuse the mHC layer's H_res producer into the kernels.
 // Differences: kernels run on PyTorch's current stream of the target device
 // (the reference uses cudaStreamPerThread), batch sizes are 64-bit, B = 0 is
 // a no-op, and a failed launch raises RuntimeError.  The Newton pair reads
@@ -306,6 +306,26 @@ py::dict birkhoff_proj_n4_hres(torch::Tensor h_res, torch::Tensor rms, py::objec
     return out;
 }
 
+// The gradient dict of the H_res functions, each gradient shaped and typed
+// like its input ("d_alpha_res" 0-d for a number; "d_b_res" 4 x 4 when b_res
+// is not given).
+py::dict hres_grads(const torch::Tensor& dh, const torch::Tensor& drms, const torch::Tensor& dalpha,
+                    const torch::Tensor& db, const torch::Tensor& h_res, const torch::Tensor& rms,
+                    const py::object& alpha_res, const torch::Tensor& b_res)
+{
+    py::dict out;
+    out["d_h_res"] = dh.reshape(h_res.sizes()).to(h_res.options());
+    out["d_rms"] = drms.reshape(rms.sizes()).to(rms.options());
+    if (py::isinstance<py::float_>(alpha_res) || py::isinstance<py::int_>(alpha_res)) {
+        out["d_alpha_res"] = dalpha.reshape({});
+    } else {
+        const torch::Tensor a = py::cast<torch::Tensor>(alpha_res);
+        out["d_alpha_res"] = dalpha.reshape(a.sizes()).to(a.options());
+    }
+    out["d_b_res"] = b_res.defined() ? db.reshape(b_res.sizes()).to(b_res.options()) : db.reshape({4, 4});
+    return out;
+}
+
 // Gradients of sum(G .* T) with T = birkhoff_proj_n4_hres(h_res, rms,
 // alpha_res, b_res): "d_h_res" (shaped like h_res), "d_rms" (like rms),
 // "d_alpha_res" (one element; 0-d for a number) and "d_b_res" (like b_res
@@ -316,8 +336,6 @@ py::dict birkhoff_proj_n4_hres_backward(torch::Tensor G, torch::Tensor T, torch:
     check_batch(G, "G");
     check_batch(T, "T", G.size(0));
     if (h_res.size(0) != G.size(0)) throw std::runtime_error("h_res must have the batch size of G");
-    const auto h_src = h_res.options();
-    const auto rms_src = rms.options();
     HResInputs in = hres_inputs(h_res, rms, alpha_res, torch::Tensor());
     const auto opts = in.h.options();
     const c10::cuda::CUDAGuard guard(in.h.device());
@@ -337,22 +355,59 @@ py::dict birkhoff_proj_n4_hres_backward(torch::Tensor G, torch::Tensor T, torch:
                                                     db.data_ptr<float>(), in.n, ws.data_ptr(), ws.numel() * 4,
                                                     current_stream()),
                  "birkhoff_proj_n4_hres_backward");
+    return hres_grads(dh, drms, dalpha, db, h_res, rms, alpha_res,
+                      kwargs.contains("b_res") ? py::cast<torch::Tensor>(kwargs["b_res"]) : torch::Tensor());
+}
+
+// Sinkhorn-Knopp on the producer's H_res activation, exp(alpha_res * h_res /
+// rms + b_res) with the producer's own exponential (no reference
+// counterpart: the reference's producer writes H_res to memory for its
+// Sinkhorn-Knopp kernel).  Arguments and conversions as birkhoff_proj_n4_hres.
+py::dict sinkhorn_knopp_n4_hres(torch::Tensor h_res, torch::Tensor rms, py::object alpha_res, torch::Tensor b_res,
+                                int max_iter, const py::kwargs&)
+{
+    const auto src = h_res.options();
+    HResInputs in = hres_inputs(h_res, rms, alpha_res, b_res);
+    const c10::cuda::CUDAGuard guard(in.h.device());
+    torch::Tensor T = torch::empty({in.n, 4, 4}, in.h.options());
+    check_status(mhc_sinkhorn_knopp_n4_hres(in.h.data_ptr<float>(), in.h.stride(0), in.rms.data_ptr<float>(),
+                                            in.alpha.data_ptr<float>(), in.b.data_ptr<float>(), T.data_ptr<float>(),
+                                            in.n, max_iter, current_stream()),
+                 "sinkhorn_knopp_n4_hres");
     py::dict out;
-    out["d_h_res"] = dh.reshape(h_res.sizes()).to(h_src);
-    out["d_rms"] = drms.reshape(rms.sizes()).to(rms_src);
-    if (py::isinstance<py::float_>(alpha_res) || py::isinstance<py::int_>(alpha_res)) {
-        out["d_alpha_res"] = dalpha.reshape({});
-    } else {
-        const torch::Tensor a = py::cast<torch::Tensor>(alpha_res);
-        out["d_alpha_res"] = dalpha.reshape(a.sizes()).to(a.options());
-    }
-    if (kwargs.contains("b_res")) {
-        const torch::Tensor b = py::cast<torch::Tensor>(kwargs["b_res"]);
-        out["d_b_res"] = db.reshape(b.sizes()).to(b.options());
-    } else {
-        out["d_b_res"] = db.reshape({4, 4});
-    }
+    out["T"] = T.to(src);
     return out;
+}
+
+// Gradients of sum(G .* T) with T = sinkhorn_knopp_n4_hres(...): the keys of
+// birkhoff_proj_n4_hres_backward.  max_iter > 20 raises ValueError.
+py::dict sinkhorn_knopp_n4_hres_backward(torch::Tensor G, torch::Tensor h_res, torch::Tensor rms,
+                                         py::object alpha_res, torch::Tensor b_res, int max_iter, const py::kwargs&)
+{
+    check_batch(G, "G");
+    if (h_res.size(0) != G.size(0)) throw std::runtime_error("h_res must have the batch size of G");
+    if (max_iter > MHC_SK_BACKWARD_MAX_ITERS)
+        throw std::invalid_argument("sinkhorn_knopp_n4_hres_backward supports max_iter <= " +
+                                    std::to_string(MHC_SK_BACKWARD_MAX_ITERS));
+    HResInputs in = hres_inputs(h_res, rms, alpha_res, b_res);
+    const auto opts = in.h.options();
+    const c10::cuda::CUDAGuard guard(in.h.device());
+    G = G.to(opts).contiguous();
+    torch::Tensor dh = torch::empty({in.n, 16}, opts);
+    torch::Tensor drms = torch::empty({in.n}, opts);
+    torch::Tensor dalpha = torch::empty({1}, opts);
+    torch::Tensor db = torch::empty({16}, opts);
+    int64_t ws_bytes = 0;
+    check_status(mhc_sinkhorn_knopp_n4_hres_backward_workspace(in.n, &ws_bytes), "sinkhorn_knopp_n4_hres_backward");
+    torch::Tensor ws = torch::empty({(ws_bytes + 3) / 4}, opts);
+    check_status(mhc_sinkhorn_knopp_n4_hres_backward(G.data_ptr<float>(), in.h.data_ptr<float>(), in.h.stride(0),
+                                                     in.rms.data_ptr<float>(), in.alpha.data_ptr<float>(),
+                                                     in.b.data_ptr<float>(), dh.data_ptr<float>(), 16,
+                                                     drms.data_ptr<float>(), dalpha.data_ptr<float>(),
+                                                     db.data_ptr<float>(), in.n, max_iter, ws.data_ptr(),
+                                                     ws.numel() * 4, current_stream()),
+                 "sinkhorn_knopp_n4_hres_backward");
+    return hres_grads(dh, drms, dalpha, db, h_res, rms, alpha_res, b_res);
 }
 
 }  // namespace
@@ -381,4 +436,10 @@ PYBIND11_MODULE(_internal, m)
     m_torch.def("birkhoff_proj_n4_hres_backward", &birkhoff_proj_n4_hres_backward, py::arg("G"), py::arg("T"),
                 py::arg("h_res"), py::arg("rms"), py::arg("alpha_res"),
                 "Gradients of birkhoff_proj_n4_hres with respect to h_res, rms, alpha_res and b_res");
+    m_torch.def("sinkhorn_knopp_n4_hres", &sinkhorn_knopp_n4_hres, py::arg("h_res"), py::arg("rms"),
+                py::arg("alpha_res"), py::arg("b_res"), py::arg("max_iter") = 20,
+                "Sinkhorn-Knopp on exp(alpha_res * h_res / rms + b_res), formed in the kernel's load");
+    m_torch.def("sinkhorn_knopp_n4_hres_backward", &sinkhorn_knopp_n4_hres_backward, py::arg("G"), py::arg("h_res"),
+                py::arg("rms"), py::arg("alpha_res"), py::arg("b_res"), py::arg("max_iter") = 20,
+                "Gradients of sinkhorn_knopp_n4_hres with respect to h_res, rms, alpha_res and b_res");
 }

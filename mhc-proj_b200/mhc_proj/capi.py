@@ -27,6 +27,9 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_hres_backward_workspace",
     "mhc_birkhoff_proj_n4_hres_backward",
     "mhc_birkhoff_proj_n4_hres_backward_noalloc",
+    "mhc_sinkhorn_knopp_n4_hres",
+    "mhc_sinkhorn_knopp_n4_hres_backward_workspace",
+    "mhc_sinkhorn_knopp_n4_hres_backward",
     "mhc_status_string",
     "mhc_abi_version",
 )
@@ -70,6 +73,10 @@ def lib() -> ctypes.CDLL:
                                                          i64, vp]
         L.mhc_birkhoff_proj_n4_hres_backward_noalloc.argtypes = [vp, vp, vp, i64, vp, vp, vp, i64, vp, vp, vp,
                                                                  i64, vp]
+        L.mhc_sinkhorn_knopp_n4_hres.argtypes = [vp, i64, vp, vp, vp, vp, i64, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_hres_backward_workspace.argtypes = [i64, ctypes.POINTER(i64)]
+        L.mhc_sinkhorn_knopp_n4_hres_backward.argtypes = [vp, vp, i64, vp, vp, vp, vp, i64, vp, vp, vp, i64, i32,
+                                                          vp, i64, vp]
         for f in _LAUNCHERS:
             getattr(L, f).restype = ctypes.c_int
         L.mhc_status_string.argtypes = [ctypes.c_int]
@@ -162,6 +169,27 @@ def birkhoff_proj_n4_hres_backward_noalloc(G: int, T: int, h: int, h_stride: int
     _check(lib().mhc_birkhoff_proj_n4_hres_backward_noalloc(G, T, h, h_stride, rms, alpha, dh, dh_stride, drms,
                                                              dalpha, db, N, stream),
            "mhc_birkhoff_proj_n4_hres_backward_noalloc")
+
+
+def sinkhorn_knopp_n4_hres(h: int, h_stride: int, rms: int, alpha: int, b: int, T: int, N: int, num_iters: int,
+                          stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_hres(h, h_stride, rms, alpha, b, T, N, num_iters, stream),
+           "mhc_sinkhorn_knopp_n4_hres")
+
+
+def sinkhorn_knopp_n4_hres_backward_workspace(N: int) -> int:
+    out = ctypes.c_int64(0)
+    _check(lib().mhc_sinkhorn_knopp_n4_hres_backward_workspace(N, ctypes.byref(out)),
+           "mhc_sinkhorn_knopp_n4_hres_backward_workspace")
+    return out.value
+
+
+def sinkhorn_knopp_n4_hres_backward(G: int, h: int, h_stride: int, rms: int, alpha: int, b: int, dh: int,
+                                    dh_stride: int, drms: int, dalpha: int, db: int, N: int, num_iters: int,
+                                    workspace: int, workspace_bytes: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_hres_backward(G, h, h_stride, rms, alpha, b, dh, dh_stride, drms, dalpha,
+                                                      db, N, num_iters, workspace, workspace_bytes, stream),
+           "mhc_sinkhorn_knopp_n4_hres_backward")
 
 
 # --- tensor conveniences ---------------------------------------------------
@@ -311,4 +339,32 @@ def birkhoff_proj_n4_hres_backward_tensor(G, T, h, rms, alpha, dh=None):
                          device=h.device)
     birkhoff_proj_n4_hres_backward(_dev(G, "G"), _dev(T, "T"), hp, hs, rp, ap, dhp, dhs, drms.data_ptr(),
                                    dalpha.data_ptr(), db.data_ptr(), n, ws.data_ptr(), ws.numel() * 4, _stream(h))
+    return dh, drms, dalpha, db
+
+
+def sinkhorn_knopp_n4_hres_tensor(h, rms, alpha, b, num_iters: int = 20):
+    """Sinkhorn-Knopp on M = exp(alpha * h / rms + b) (the producer's H_res), formed in the kernel's load."""
+    import torch
+
+    hp, hs, rp, ap, bp = _hres_inputs(h, rms, alpha, b)
+    T = torch.empty(h.shape[0], 4, 4, dtype=torch.float32, device=h.device)
+    sinkhorn_knopp_n4_hres(hp, hs, rp, ap, bp, T.data_ptr(), h.shape[0], num_iters, _stream(h))
+    return T
+
+
+def sinkhorn_knopp_n4_hres_backward_tensor(G, h, rms, alpha, b, num_iters: int = 20, dh=None):
+    """Gradients (dh, drms, dalpha, db) of sinkhorn_knopp_n4_hres."""
+    import torch
+
+    hp, hs, rp, ap, bp = _hres_inputs(h, rms, alpha, b)
+    n = h.shape[0]
+    if dh is None:
+        dh = torch.empty(n, 16, dtype=torch.float32, device=h.device)
+    dhp, dhs, _, _, _ = _hres_inputs(dh, rms, alpha, b)
+    drms = torch.empty(n, dtype=torch.float32, device=h.device)
+    dalpha = torch.empty((), dtype=torch.float32, device=h.device)
+    db = torch.empty(4, 4, dtype=torch.float32, device=h.device)
+    ws = torch.empty(sinkhorn_knopp_n4_hres_backward_workspace(n) // 4, dtype=torch.float32, device=h.device)
+    sinkhorn_knopp_n4_hres_backward(_dev(G, "G"), hp, hs, rp, ap, bp, dhp, dhs, drms.data_ptr(), dalpha.data_ptr(),
+                                    db.data_ptr(), n, num_iters, ws.data_ptr(), ws.numel() * 4, _stream(h))
     return dh, drms, dalpha, db

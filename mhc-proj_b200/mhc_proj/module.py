@@ -146,14 +146,67 @@ class MHCProjectionN4HRes(nn.Module):
         self.tol = tol
 
     def forward(self, h_res, rms, alpha_res, b_res):
-        if h_res.shape[-1] == 16:
-            lead = h_res.shape[:-1]
-        elif h_res.ndim >= 2 and h_res.shape[-2:] == (4, 4):
-            lead = h_res.shape[:-2]
-        else:
-            raise ValueError("h_res must be a tensor of size ... x 16 or ... x 4 x 4")
-        if tuple(rms.shape) != tuple(lead):
-            raise ValueError("rms must have the leading shape of h_res")
+        _hres_lead(h_res, rms)
         if not torch.is_tensor(alpha_res):
             alpha_res = torch.tensor(float(alpha_res), dtype=torch.float32, device=h_res.device)
         return MHCProjectionN4HResFunction.apply(h_res, rms, alpha_res, b_res, self.tol)
+
+
+class MHCSinkhornN4HResFunction(torch.autograd.Function):
+    """T = sinkhorn_knopp_n4(exp(alpha_res * h_res / rms + b_res)) with the
+    producer's own exponential formed in the kernel's load; gradients for
+    all four inputs from one fused backward kernel plus the batch fold."""
+
+    @staticmethod
+    def forward(ctx, h_res, rms, alpha_res, b_res, max_iter=20):
+        lead = rms.shape
+        h2 = h_res.reshape(-1, 16)
+        T = _internal.torch.sinkhorn_knopp_n4_hres(h2, rms.reshape(-1), alpha_res, b_res, max_iter)["T"]
+        ctx.save_for_backward(h2, rms, alpha_res, b_res)
+        ctx.h_shape = h_res.shape
+        ctx.max_iter = max_iter
+        ctx.set_materialize_grads(False)
+        return T.view(*lead, 4, 4)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        if grad_output is None or not any(ctx.needs_input_grad[:4]):
+            return None, None, None, None, None
+        h2, rms, alpha_res, b_res = ctx.saved_tensors
+        g = _internal.torch.sinkhorn_knopp_n4_hres_backward(grad_output.reshape(-1, 4, 4), h2, rms.reshape(-1),
+                                                            alpha_res, b_res, ctx.max_iter)
+        need = ctx.needs_input_grad
+        return (g["d_h_res"].view(ctx.h_shape) if need[0] else None,
+                g["d_rms"].view(rms.shape) if need[1] else None,
+                g["d_alpha_res"] if need[2] else None,
+                g["d_b_res"] if need[3] else None,
+                None)
+
+
+def _hres_lead(h_res, rms):
+    if h_res.shape[-1] == 16:
+        lead = h_res.shape[:-1]
+    elif h_res.ndim >= 2 and h_res.shape[-2:] == (4, 4):
+        lead = h_res.shape[:-2]
+    else:
+        raise ValueError("h_res must be a tensor of size ... x 16 or ... x 4 x 4")
+    if tuple(rms.shape) != tuple(lead):
+        raise ValueError("rms must have the leading shape of h_res")
+
+
+class MHCSinkhornN4HRes(nn.Module):
+    """Sinkhorn-Knopp fused with the mHC layer's H_res producer: the same T as
+    the reference's producer (fused_h_activations, src/utils.cuh:50-127) writing
+    H_res = exp(alpha_res * h_res / rms + b_res) followed by its
+    sinkhorn_knopp_n4, without H_res in memory.  forward(h_res, rms,
+    alpha_res, b_res) as MHCProjectionN4HRes; returns (..., 4, 4)."""
+
+    def __init__(self, max_iter=20):
+        super().__init__()
+        self.max_iter = max_iter
+
+    def forward(self, h_res, rms, alpha_res, b_res):
+        _hres_lead(h_res, rms)
+        if not torch.is_tensor(alpha_res):
+            alpha_res = torch.tensor(float(alpha_res), dtype=torch.float32, device=h_res.device)
+        return MHCSinkhornN4HResFunction.apply(h_res, rms, alpha_res, b_res, self.max_iter)

@@ -266,3 +266,118 @@ def test_cuda_graph_capture(producer):
     assert bitwise_equal(T, T0)
     for k in ("d_h_res", "d_rms", "d_alpha_res", "d_b_res"):
         assert bitwise_equal(g[k], g0[k])
+
+
+# --- the producer fused with Sinkhorn-Knopp ---------------------------------
+
+def ref_producer_hres(producer, H, rms, alpha, b):
+    """The reference producer's H_res (its exp of the pre-activation), (n, 4, 4)."""
+    n = H.shape[0]
+    pre = torch.empty(n, 4, device="cuda")
+    post = torch.empty(n, 4, device="cuda")
+    M = torch.empty(n, 4, 4, device="cuda")
+    z = torch.zeros(4, device="cuda")
+    producer.fused_h_activations_n4(pre.data_ptr(), post.data_ptr(), M.data_ptr(), H.data_ptr(), rms.data_ptr(),
+                                    1.0, 1.0, alpha, z.data_ptr(), z.data_ptr(), b.data_ptr(), n, stream())
+    return M
+
+
+@pytest.mark.parametrize("n", [1, 33, 65537, (1 << 20) + 3])
+@pytest.mark.parametrize("alpha", [0.05, 1.0])
+@pytest.mark.parametrize("iters", [0, 1, 20])
+def test_sk_fused_forward_is_the_reference_producer_then_sk(ref, producer, n, alpha, iters):
+    H, h, rms, a, b = layer_inputs(n, 30 + n % 89, alpha=alpha)
+    T = capi.sinkhorn_knopp_n4_hres_tensor(h, rms, a, b, iters)
+    M = ref_producer_hres(producer, H, rms, alpha, b)
+    Tr = torch.empty_like(M)
+    ref.sinkhorn_knopp_n4(M.data_ptr(), Tr.data_ptr(), n, iters, stream())
+    torch.cuda.synchronize()
+    assert bitwise_equal(T, Tr)
+    if iters == 0:
+        assert bitwise_equal(T, M)
+
+
+def test_sk_fused_forward_layouts(ref, producer):
+    n = 40001
+    H, h, rms, a, b = layer_inputs(n, 31, alpha=0.7)
+    M = ref_producer_hres(producer, H, rms, 0.7, b)
+    Tr = torch.empty_like(M)
+    ref.sinkhorn_knopp_n4(M.data_ptr(), Tr.data_ptr(), n, 20, stream())
+    H21 = torch.zeros(n, 21, device="cuda")
+    H21[:, 5:21] = h
+    T21 = capi.sinkhorn_knopp_n4_hres_tensor(H21[:, 5:21], rms, a, b)
+    Td = capi.sinkhorn_knopp_n4_hres_tensor(h.contiguous().view(n, 4, 4), rms, a, b)
+    torch.cuda.synchronize()
+    assert bitwise_equal(T21, Tr) and bitwise_equal(Td, Tr)
+
+
+@pytest.mark.parametrize("n,iters", [(1, 20), (257, 20), (100003, 20), (100003, 5), (1 << 20, 20)])
+def test_sk_fused_backward_against_the_unfused_gradient(producer, n, iters):
+    alpha = 0.8
+    H, h, rms, a, b = layer_inputs(n, 40 + n % 7, alpha=alpha)
+    G = torch.randn(n, 4, 4, device="cuda", generator=torch.Generator(device="cuda").manual_seed(6))
+    dh, drms, dalpha, db = capi.sinkhorn_knopp_n4_hres_backward_tensor(G, h, rms, a, b, iters)
+    M = ref_producer_hres(producer, H, rms, alpha, b)
+    dM = capi.sinkhorn_knopp_n4_backward_tensor(G, M, iters)  # the exact VJP of the plain kernel
+    dR = dM * M  # what the fused kernel forms, rounded the same way
+    torch.cuda.synchronize()
+    check_against_chain(dR, h, rms, alpha, dh, drms, dalpha, db)
+
+
+def test_sk_fused_backward_checks_and_empty_batch(producer):
+    n = 1000
+    H, h, rms, a, b = layer_inputs(n, 41)
+    G = torch.randn(n, 4, 4, device="cuda")
+    r1 = capi.sinkhorn_knopp_n4_hres_backward_tensor(G, h, rms, a, b)
+    r2 = capi.sinkhorn_knopp_n4_hres_backward_tensor(G, h, rms, a, b)
+    torch.cuda.synchronize()
+    for x, y in zip(r1, r2):
+        assert bitwise_equal(x, y)
+    dh, drms, dalpha, db = (torch.empty(n, 16, device="cuda"), torch.empty(n, device="cuda"),
+                            torch.empty((), device="cuda"), torch.empty(4, 4, device="cuda"))
+    need = capi.sinkhorn_knopp_n4_hres_backward_workspace(n)
+    assert need == 8 * 17 * 4  # ceil(1000 / 128) blocks of 17 partial sums
+    ws = torch.empty(need // 4, device="cuda")
+    args = [G.data_ptr(), h.data_ptr(), 24, rms.data_ptr(), a.data_ptr(), b.data_ptr(), dh.data_ptr(), 16,
+            drms.data_ptr(), dalpha.data_ptr(), db.data_ptr(), n]
+    with pytest.raises(capi.MhcError) as e:
+        capi.sinkhorn_knopp_n4_hres_backward(*args, 20, ws.data_ptr(), need - 4, stream())
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+    with pytest.raises(capi.MhcError) as e:
+        capi.sinkhorn_knopp_n4_hres_backward(*args, 21, ws.data_ptr(), need, stream())
+    assert e.value.code == capi.MHC_ERR_ITERS
+    with pytest.raises(ValueError):
+        mhc_proj.torch.sinkhorn_knopp_n4_hres_backward(G, h, rms, a, b, max_iter=21)
+    E = torch.empty(0, 24, device="cuda")
+    z = capi.sinkhorn_knopp_n4_hres_backward_tensor(torch.empty(0, 4, 4, device="cuda"), E[:, 8:24],
+                                                    torch.empty(0, device="cuda"), a, b)
+    torch.cuda.synchronize()
+    assert float(z[2]) == 0.0 and bool((z[3] == 0).all())
+
+
+def test_sk_module_autograd(producer):
+    n = 4096
+    H, h, rms, a, b = layer_inputs(n, 42, alpha=0.6)
+    Hp = H.clone().requires_grad_(True)
+    rp = rms.clone().requires_grad_(True)
+    ap = torch.nn.Parameter(torch.tensor(0.6, device="cuda"))
+    bp = torch.nn.Parameter(b.clone().view(4, 4))
+    G = torch.randn(n, 4, 4, device="cuda")
+    T = mhc_proj.MHCSinkhornN4HRes(max_iter=20)(Hp[:, 8:24], rp, ap, bp)
+    (T * G).sum().backward()
+    T2 = capi.sinkhorn_knopp_n4_hres_tensor(h, rms, a, b)
+    dh, drms, dalpha, db = capi.sinkhorn_knopp_n4_hres_backward_tensor(G, h, rms, a, b)
+    torch.cuda.synchronize()
+    assert bitwise_equal(T.detach(), T2)
+    assert bitwise_equal(Hp.grad[:, 8:24], dh) and bool((Hp.grad[:, :8] == 0).all())
+    assert bitwise_equal(rp.grad, drms) and bitwise_equal(ap.grad, dalpha) and bitwise_equal(bp.grad, db)
+    # the vanilla Sinkhorn on the float64 producer output agrees to the kernels' eps semantics
+    with torch.enable_grad():
+        h64 = h.double().requires_grad_(True)
+        P = torch.exp(0.6 * h64.reshape(n, 4, 4) / rms.double()[:, None, None] + b.double().view(4, 4))
+        for _ in range(20):
+            P = P / P.sum(2, keepdim=True)
+            P = P / P.sum(1, keepdim=True)
+        (P * G.double()).sum().backward()
+    assert torch.allclose(T.double(), P.detach(), atol=1e-5)
+    assert torch.allclose(Hp.grad[:, 8:24].double(), h64.grad, atol=1e-4, rtol=1e-4)
