@@ -41,6 +41,7 @@ BYTES_FWD = 128      # R in (64 B) + T out (64 B) per matrix
 BYTES_BWD = 192      # G, T in + D out per matrix
 BYTES_HRES_FWD = 132  # h (64 B of a 96 B row) + rms in, T out
 BYTES_HRES_BWD = 264  # G, T, h, rms in; dh, drms out
+BYTES_SKHRES_BWD = 200  # G, h, rms in; dh, drms out (M is recomputed from h)
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -50,10 +51,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["newton", "sinkhorn", "hres"], default="newton",
+    ap.add_argument("--workload", choices=["newton", "sinkhorn", "hres", "sk_hres"], default="newton",
                     help="newton: the Newton forward + IFT backward (default, the headline metric); "
                          "sinkhorn: the fused exp + Sinkhorn-Knopp pair, 20 iterations; "
-                         "hres: the projection fused with the mHC layer's H_res producer, forward + backward")
+                         "hres: the projection fused with the mHC layer's H_res producer, forward + backward; "
+                         "sk_hres: the Sinkhorn-Knopp pair (20 iterations) fused with that producer")
     ap.add_argument("--n", type=int, default=None, help="matrices per GPU (default 2^24, or 2^22 for sinkhorn)")
     ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
     ap.add_argument("--tol", type=float, default=1e-6)
@@ -102,6 +104,9 @@ def sm_count(dev):
 def workload_config(args, world):
     if args.workload == "sinkhorn":
         what = "fused exp + Sinkhorn-Knopp n4 (20 iterations) forward + backward"
+    elif args.workload == "sk_hres":
+        what = ("H_res producer (exp(alpha*h/rms+b), h = columns 8..23 of an [N,24] projection) fused with "
+                "Sinkhorn-Knopp n4 (20 iterations) forward + fused backward incl. dalpha, db batch sums")
     elif args.workload == "hres":
         what = (f"H_res producer (alpha*h/rms+b, h = columns 8..23 of an [N,24] projection) fused with the Newton "
                 f"forward (tol {args.tol:g}) + fused backward incl. dalpha, db batch sums")
@@ -297,6 +302,11 @@ def run_ours(args):
     if args.workload == "sinkhorn":
         fwd = lambda: mhc_proj.torch.sinkhorn_knopp_n4_logits(R, 20)["T"]  # noqa: E731
         bwd = lambda T: mhc_proj.torch.sinkhorn_knopp_n4_logits_backward(G, R, 20)["D"]  # noqa: E731
+    elif args.workload == "sk_hres":
+        hres = hres_inputs(R, rank, dev)
+        h, rms, a, b = hres
+        fwd = lambda: mhc_proj.torch.sinkhorn_knopp_n4_hres(h, rms, a, b, 20)["T"]  # noqa: E731
+        bwd = lambda T: mhc_proj.torch.sinkhorn_knopp_n4_hres_backward(G, h, rms, a, b, 20)  # noqa: E731
     elif args.workload == "hres":
         hres = hres_inputs(R, rank, dev)
         h, rms, a, b = hres
@@ -346,6 +356,8 @@ def run_ours(args):
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
     if args.workload == "hres":
         unfused_ms, plain_fwd_ms = hres_unfused_ms(hres, G, tol, args.steps)
+    if args.workload == "sk_hres":
+        unfused_ms = sk_hres_unfused_ms(hres, G, args.steps)
 
     stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
     per_rank = [stats.clone()]
@@ -445,6 +457,26 @@ def run_ours(args):
                        "dh, drms, dalpha, db with torch ops (this repository's unfused kernels)",
                 "plain_forward_ms": plain_fwd_ms,
                 "plain_forward_how": "birkhoff_proj_n4 alone on the same logits materialised in HBM"}
+        if args.workload == "sk_hres":
+            fwd_gbs = BYTES_HRES_FWD * n / (fwd_ms * 1e-3) / 1e9
+            bwd_gbs = BYTES_SKHRES_BWD * n / (bwd_ms * 1e-3) / 1e9
+            step_gbs = (BYTES_HRES_FWD + BYTES_SKHRES_BWD) * n / (ms_per_step * 1e-3) / 1e9
+            line["metric"] = "H_res producer + Sinkhorn-Knopp n4 (20 iterations) fwd+bwd matrices/s"
+            line["roofline"].update({
+                "kernel": "sk_fwd_kernel<HResInput> (producer fused into the Sinkhorn-Knopp forward)",
+                "achieved": fwd_gbs, "frac": fwd_gbs / peak, "algorithmic_bytes_per_matrix": BYTES_HRES_FWD,
+                "traffic": None, "compute": None,
+                "step": {"achieved": step_gbs, "frac": step_gbs / peak,
+                         "algorithmic_bytes_per_matrix": BYTES_HRES_FWD + BYTES_SKHRES_BWD},
+                "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms, "forward_gbs": fwd_gbs,
+                            "backward_gbs": bwd_gbs, "backward_frac": bwd_gbs / peak,
+                            "backward_kernels": "sk_hres_bwd_kernel + partial_sums_fold_kernel"}})
+            line["e2e"] = None
+            line["gpu_launches"] = 3 * args.steps
+            line["unfused_composition"] = {
+                "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
+                "how": "H_res = exp(alpha*h/rms + b) with torch ops, sinkhorn_knopp_n4, sinkhorn_knopp_n4_backward, "
+                       "then dR = dM*M and dh, drms, dalpha, db with torch ops (this repository's unfused kernels)"}
         if world == 1 and not args.no_cpu_baseline and args.workload == "newton":
             rate, nt, done = cpu_port_rate(args.cpu_seconds, 1 << 18, args.dist, tol)
             line["cpu_baseline"] = {
@@ -513,6 +545,37 @@ def hres_unfused_ms(hres, G, tol, steps):
     R = (a * h / rms[:, None] + b).reshape(n, 4, 4)
     plain_fwd = timed(lambda: mhc_proj.torch.birkhoff_proj_n4(R, tol))
     return timed(once), plain_fwd
+
+
+def sk_hres_unfused_ms(hres, G, steps):
+    """Device time of the sk_hres step as separate kernels: the producer and
+    the chain rule as torch ops around the plain Sinkhorn-Knopp kernels."""
+    import torch
+
+    import mhc_proj
+
+    h, rms, a, b = hres
+    n = h.shape[0]
+
+    def once():
+        M = torch.exp(a * h / rms[:, None] + b).reshape(n, 4, 4)
+        mhc_proj.torch.sinkhorn_knopp_n4(M, 20)
+        dR = (mhc_proj.torch.sinkhorn_knopp_n4_backward(G, M, 20)["D"] * M).reshape(n, 16)
+        s = a / rms
+        q = (dR * h).sum(1)
+        return dR * s[:, None], -(s / rms) * q, (q / rms).sum(), dR.sum(0)
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def sinkhorn_unfused_ms(R, G, steps):
@@ -598,7 +661,7 @@ def run_e2e(args, R, G, dev, world):
 def main():
     args = parse_args()
     if args.n is None:
-        args.n = (1 << 22) if args.workload == "sinkhorn" else (1 << 24)
+        args.n = (1 << 22) if args.workload in ("sinkhorn", "sk_hres") else (1 << 24)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
