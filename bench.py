@@ -447,7 +447,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_matrix": BYTES_HRES_FWD + BYTES_HRES_BWD},
                 "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms, "forward_gbs": fwd_gbs,
                             "backward_gbs": bwd_gbs, "backward_frac": bwd_gbs / peak,
-                            "backward_kernels": "birkhoff_hres_bwd_kernel + hres_reduce_kernel"}})
+                            "backward_kernels": "birkhoff_hres_bwd_kernel + partial_sums_fold_kernel"}})
             line["roofline"]["compute"] = None
             line["e2e"] = None
             line["gpu_launches"] = 3 * args.steps
