@@ -69,6 +69,22 @@ MHC_API int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_
 MHC_API int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float tol, int64_t N,
                                        int32_t* d_iters, float* d_gnorm, cudaStream_t stream);
 
+/* mhc_birkhoff_proj_n4 that also writes, per matrix, the final dual beta
+ * (4 floats at d_beta + 4k, beta[3] = 0 up to its sign): T is exactly
+ * row-softmax(beta + R), which mhc_birkhoff_proj_n4_backward_duals rebuilds
+ * bit for bit, so a caller may keep R and 16 bytes of beta per matrix for the
+ * backward instead of T's 64.  T is the same as from mhc_birkhoff_proj_n4.
+ * No reference counterpart. */
+MHC_API int mhc_birkhoff_proj_n4_duals(const float* d_R, float* d_T, float* d_beta, float tol,
+                                       int64_t N, cudaStream_t stream);
+
+/* mhc_birkhoff_proj_n4_backward from R and the saved beta instead of T (T is
+ * rebuilt in registers with the forward's arithmetic); D is the same bits.
+ * Reads G, R and beta (208 bytes per matrix) instead of G and T (192).  No
+ * reference counterpart. */
+MHC_API int mhc_birkhoff_proj_n4_backward_duals(const float* d_G, const float* d_R, const float* d_beta,
+                                                float* d_D, int64_t N, cudaStream_t stream);
+
 /* mhc_birkhoff_proj_n4 on a strided batch of any storage type: matrix k of R
  * starts at element k * r_stride (its 16 entries row-major and contiguous),
  * T is written contiguous in the same type.  No reference counterpart: the

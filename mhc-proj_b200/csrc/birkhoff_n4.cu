@@ -69,6 +69,18 @@ struct HResSource {
     }
 };
 
+// Four floats at p (16-byte aligned when kVec).
+template <bool kVec>
+__device__ __forceinline__ void store_vec4(float* p, const float (&v)[4])
+{
+    if constexpr (kVec) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) p[j] = v[j];
+    }
+}
+
 // Newton forward, persistent.  Warp w owns matrices [w*per_warp, ...) of the
 // batch.  Each lane runs the reference algorithm (birkhoff_proj_n4.cu:375-499)
 // for one matrix as a state machine, and a lane that finishes stores its T and
@@ -101,13 +113,15 @@ struct HResSource {
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
 // kStats: also write, per matrix, the number of Newton iterations taken and
-// the final gradient l1 norm (a separate instantiation; the plain one carries
-// no cost for it).
-template <class Rd, class Src, class Elem, bool kVec, bool kStats = false>
+// the final gradient l1 norm; kDuals: also write the final beta (4 floats,
+// the point whose T is the output: T = row-softmax(beta + R)).  Separate
+// instantiations; the plain one carries no cost for either.
+template <class Rd, class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
 __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_warp,
                                                                     int32_t* __restrict__ iters_out = nullptr,
-                                                                    float* __restrict__ gnorm_out = nullptr)
+                                                                    float* __restrict__ gnorm_out = nullptr,
+                                                                    float* __restrict__ beta_out = nullptr)
 {
     using Prod = typename Rd::P;
     const int lane = threadIdx.x & 31;
@@ -123,6 +137,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         iters_out += begin;
         gnorm_out += begin;
     }
+    if constexpr (kDuals) beta_out += begin * 4;
 
     Mat4 r;                 // logits of the lane's matrix
     float p[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // Gram sums of T at the current point
@@ -275,6 +290,11 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
                 gnorm_out[idx] = gn;
             }
         }
+        if constexpr (kDuals) {
+            // beta of the output's point: the adopted one (an exit after a
+            // column pass keeps the beta = 0 of the evaluation that wrote T)
+            if (done) store_vec4<kVec>(beta_out + static_cast<int64_t>(idx) * 4, beta);
+        }
         // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);
         if (want) {
@@ -294,6 +314,50 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             }
         }
     }
+}
+
+// T = row-softmax(beta + R) with the forward's arithmetic, so that a T
+// rebuilt from the saved beta is the forward's output bit for bit.
+__device__ __forceinline__ void rebuild_t(const Mat4& r, const float (&beta)[4], Mat4& T)
+{
+    float X[16], e[16], s[4], lse[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) X[4 * l + q] = beta[q] + r.m[4 * l + q];
+    lse_pass(X, e, s, lse);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float rs = fast_rcp(s[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) T.m[4 * i + j] = __fmul_rn(e[4 * i + j], rs);
+    }
+}
+
+// The IFT backward from the saved duals instead of T: T is rebuilt from R and
+// beta (16 bytes per matrix saved instead of 64), then D as from T.
+template <class Rd, bool kVec>
+__global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_duals_kernel(const float* __restrict__ G,
+                                                                            const float* __restrict__ R,
+                                                                            const float* __restrict__ beta,
+                                                                            float* __restrict__ D, int64_t N)
+{
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= N) return;
+    Mat4 g, r, t, d;
+    float b[4];
+    load_mat<kVec>(R, idx, r);
+    if constexpr (kVec) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(beta) + idx);
+        b[0] = v.x, b[1] = v.y, b[2] = v.z, b[3] = v.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = __ldg(beta + idx * 4 + j);
+    }
+    rebuild_t(r, b, t);
+    load_mat<kVec>(G, idx, g);
+    ift_backward<Rd>(g, t, d);
+    store_mat<kVec>(D, idx, d);
 }
 
 // One thread per matrix.  G and T may have different storage types and batch
@@ -371,11 +435,11 @@ static int64_t forward_warp_slots()
     return slots;
 }
 
-template <class Src, class Elem, bool kVec, bool kStats = false>
+template <class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
 static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters = nullptr,
-                          float* gnorm = nullptr)
+                          float* gnorm = nullptr, float* beta = nullptr)
 {
-    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats>;
+    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats, kDuals>;
     const int64_t slots = forward_warp_slots<kernel>();
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
@@ -387,7 +451,7 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     const int64_t per_warp = ceil_div(N, warps);
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
-    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm);
+    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm, beta);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -611,6 +675,31 @@ extern "C" int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, cons
     }
     return hres_backward_launch(d_G, d_T, d_h, h_stride, d_rms, d_alpha, d_dh, dh_stride, d_drms, d_dalpha, d_db, N,
                                 partials, blocks, stream);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_duals(const float* d_R, float* d_T, float* d_beta, float tol, int64_t N,
+                                          cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_R || !d_T || !d_beta))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    return aligned16(d_R) && aligned16(d_T) && aligned16(d_beta)
+               ? launch_forward<DenseSource<float, true>, float, true, false, true>({d_R, 16}, d_T, tol, N, stream,
+                                                                                    nullptr, nullptr, d_beta)
+               : launch_forward<DenseSource<float, false>, float, false, false, true>({d_R, 16}, d_T, tol, N, stream,
+                                                                                      nullptr, nullptr, d_beta);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_backward_duals(const float* d_G, const float* d_R, const float* d_beta,
+                                                   float* d_D, int64_t N, cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_G || !d_R || !d_beta || !d_D))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    const int64_t grid = ceil_div(N, kBackwardBlock);
+    if (aligned16(d_G) && aligned16(d_R) && aligned16(d_beta) && aligned16(d_D))
+        birkhoff_bwd_duals_kernel<RefRounding, true><<<grid, kBackwardBlock, 0, stream>>>(d_G, d_R, d_beta, d_D, N);
+    else
+        birkhoff_bwd_duals_kernel<RefRounding, false><<<grid, kBackwardBlock, 0, stream>>>(d_G, d_R, d_beta, d_D, N);
+    return static_cast<int>(cudaGetLastError());
 }
 
 extern "C" const char* mhc_status_string(int status)

@@ -102,10 +102,32 @@ py::dict birkhoff_proj_n4_stats(torch::Tensor R, float tol)
     return out;
 }
 
+// return_duals=True (an optional keyword) adds "beta" (B x 4 fp32: the final
+// duals, T = row-softmax(beta + R)), for birkhoff_proj_n4_backward_duals.
+py::dict birkhoff_proj_n4_duals(torch::Tensor R, float tol)
+{
+    const auto src = R.options();
+    const auto opts = target_options(R);
+    R = R.to(opts);
+    const c10::cuda::CUDAGuard guard(R.device());
+    R = R.contiguous();
+    const int64_t n = R.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, opts);
+    torch::Tensor beta = torch::empty({n, 4}, opts);
+    check_status(mhc_birkhoff_proj_n4_duals(R.data_ptr<float>(), T.data_ptr<float>(), beta.data_ptr<float>(), tol, n,
+                                            current_stream()),
+                 "birkhoff_proj_n4");
+    py::dict out;
+    out["T"] = T.to(src);
+    out["beta"] = beta;
+    return out;
+}
+
 py::dict birkhoff_proj_n4(torch::Tensor R, float tol, const py::kwargs& kwargs)
 {
     check_batch(R, "R");
     if (kwargs.contains("return_stats") && py::cast<bool>(kwargs["return_stats"])) return birkhoff_proj_n4_stats(R, tol);
+    if (kwargs.contains("return_duals") && py::cast<bool>(kwargs["return_duals"])) return birkhoff_proj_n4_duals(R, tol);
     if (native_batch(R)) {
         // fp32/bf16/fp16 at any batch stride: read in place, T in R's type
         const c10::cuda::CUDAGuard guard(R.device());
@@ -159,6 +181,33 @@ py::dict birkhoff_proj_n4_backward(torch::Tensor G, torch::Tensor T, const py::k
     check_status(mhc_birkhoff_proj_n4_backward(G.data_ptr<float>(), T.data_ptr<float>(), D.data_ptr<float>(), n,
                                                current_stream()),
                  "birkhoff_proj_n4_backward");
+    py::dict out;
+    out["D"] = D.to(src);
+    return out;
+}
+
+// The IFT backward from the logits R and the duals beta that
+// birkhoff_proj_n4(R, return_duals=True) returned, instead of T (no reference
+// counterpart).  D is converted to G's dtype/device like the T-based backward.
+py::dict birkhoff_proj_n4_backward_duals(torch::Tensor G, torch::Tensor R, torch::Tensor beta, const py::kwargs&)
+{
+    check_batch(G, "G");
+    check_batch(R, "R", G.size(0));
+    if (beta.numel() != 4 * G.size(0)) throw std::runtime_error("beta must be a tensor of size B x 4");
+    const auto src = G.options();
+    const auto opts = target_options(G);
+    G = G.to(opts);
+    R = R.to(opts);
+    beta = beta.to(opts);
+    const c10::cuda::CUDAGuard guard(G.device());
+    G = G.contiguous();
+    R = R.contiguous();
+    beta = beta.contiguous();
+    const int64_t n = G.size(0);
+    torch::Tensor D = torch::empty({n, 4, 4}, opts);
+    check_status(mhc_birkhoff_proj_n4_backward_duals(G.data_ptr<float>(), R.data_ptr<float>(), beta.data_ptr<float>(),
+                                                     D.data_ptr<float>(), n, current_stream()),
+                 "birkhoff_proj_n4_backward_duals");
     py::dict out;
     out["D"] = D.to(src);
     return out;
@@ -421,6 +470,8 @@ PYBIND11_MODULE(_internal, m)
                 "KL projection of 4x4 matrices onto the Birkhoff polytope");
     m_torch.def("birkhoff_proj_n4_backward", &birkhoff_proj_n4_backward, py::arg("G"), py::arg("T"),
                 "KL projection of 4x4 matrices onto the Birkhoff polytope, backward pass");
+    m_torch.def("birkhoff_proj_n4_backward_duals", &birkhoff_proj_n4_backward_duals, py::arg("G"), py::arg("R"),
+                py::arg("beta"), "Backward of birkhoff_proj_n4 from R and its saved duals instead of T");
     m_torch.def("sinkhorn_knopp_n4", &sinkhorn_knopp_n4, py::arg("M"), py::arg("max_iter") = 20,
                 "Sinkhorn-Knopp algorithm for 4x4 matrices");
     m_torch.def("sinkhorn_knopp_n4_backward", &sinkhorn_knopp_n4_backward, py::arg("G"), py::arg("M"),

@@ -19,6 +19,8 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_ex",
     "mhc_birkhoff_proj_n4_backward_ex",
     "mhc_birkhoff_proj_n4_stats",
+    "mhc_birkhoff_proj_n4_duals",
+    "mhc_birkhoff_proj_n4_backward_duals",
     "mhc_sinkhorn_knopp_n4",
     "mhc_sinkhorn_knopp_n4_backward",
     "mhc_sinkhorn_knopp_n4_logits",
@@ -65,6 +67,8 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_ex.argtypes = [vp, i64, vp, i32, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_backward_ex.argtypes = [vp, i64, i32, vp, i64, i32, vp, i64, vp]
         L.mhc_birkhoff_proj_n4_stats.argtypes = [vp, vp, f32, i64, vp, vp, vp]
+        L.mhc_birkhoff_proj_n4_duals.argtypes = [vp, vp, vp, f32, i64, vp]
+        L.mhc_birkhoff_proj_n4_backward_duals.argtypes = [vp, vp, vp, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
         L.mhc_birkhoff_proj_n4_hres.argtypes = [vp, i64, vp, vp, vp, vp, f32, i64, vp]
@@ -110,6 +114,14 @@ def birkhoff_proj_n4_backward(G: int, T: int, D: int, N: int, stream: int = 0) -
 
 def birkhoff_proj_n4_stats(R: int, T: int, tol: float, N: int, iters: int, gnorm: int, stream: int = 0) -> None:
     _check(lib().mhc_birkhoff_proj_n4_stats(R, T, tol, N, iters, gnorm, stream), "mhc_birkhoff_proj_n4_stats")
+
+
+def birkhoff_proj_n4_duals(R: int, T: int, beta: int, tol: float, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_duals(R, T, beta, tol, N, stream), "mhc_birkhoff_proj_n4_duals")
+
+
+def birkhoff_proj_n4_backward_duals(G: int, R: int, beta: int, D: int, N: int, stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_backward_duals(G, R, beta, D, N, stream), "mhc_birkhoff_proj_n4_backward_duals")
 
 
 def birkhoff_proj_n4_ex(R: int, r_stride: int, T: int, dtype: int, tol: float, N: int, stream: int = 0) -> None:
@@ -222,6 +234,27 @@ def birkhoff_proj_n4_backward_tensor(G, T, out=None):
 
     D = torch.empty_like(G) if out is None else out
     birkhoff_proj_n4_backward(_dev(G, "G"), _dev(T, "T"), _dev(D, "D"), G.shape[0], _stream(G))
+    return D
+
+
+def birkhoff_proj_n4_duals_tensor(R, tol: float = 1e-6):
+    """(T, beta): the forward and its final duals, beta (N, 4)."""
+    import torch
+
+    T = torch.empty_like(R)
+    beta = torch.empty(R.shape[0], 4, dtype=torch.float32, device=R.device)
+    birkhoff_proj_n4_duals(_dev(R, "R"), _dev(T, "T"), beta.data_ptr(), tol, R.shape[0], _stream(R))
+    return T, beta
+
+
+def birkhoff_proj_n4_backward_duals_tensor(G, R, beta):
+    import torch
+
+    D = torch.empty_like(G)
+    if not (beta.is_cuda and beta.dtype == torch.float32 and beta.is_contiguous() and beta.numel() == 4 * G.shape[0]):
+        raise ValueError("beta must be a contiguous float32 CUDA tensor of N x 4 elements")
+    birkhoff_proj_n4_backward_duals(_dev(G, "G"), _dev(R, "R"), beta.data_ptr(), _dev(D, "D"), G.shape[0],
+                                    _stream(G))
     return D
 
 

@@ -24,35 +24,50 @@ from . import _internal
 
 class MHCProjectionN4Function(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, R, tol=1e-6):
+    def forward(ctx, R, tol=1e-6, save_duals=False):
         in_shape = R.shape
         R = R.reshape(-1, 4, 4)
-        T = _internal.torch.birkhoff_proj_n4(R, tol)["T"]
-        ctx.save_for_backward(T)
+        ctx.save_duals = save_duals
+        if save_duals:
+            out = _internal.torch.birkhoff_proj_n4(R, tol, return_duals=True)
+            T = out["T"]
+            ctx.save_for_backward(R, out["beta"])
+        else:
+            T = _internal.torch.birkhoff_proj_n4(R, tol)["T"]
+            ctx.save_for_backward(T)
         ctx.set_materialize_grads(False)
         return T.view(in_shape)
 
     @staticmethod
     def backward(ctx, grad_output):
         if not ctx.needs_input_grad[0] or grad_output is None:
-            return None, None
+            return None, None, None
         in_shape = grad_output.shape
         G = grad_output.reshape(-1, 4, 4)
-        (T,) = ctx.saved_tensors
-        D = _internal.torch.birkhoff_proj_n4_backward(G, T)["D"]
-        return D.view(in_shape), None
+        if ctx.save_duals:
+            R, beta = ctx.saved_tensors
+            D = _internal.torch.birkhoff_proj_n4_backward_duals(G, R, beta)["D"]
+        else:
+            (T,) = ctx.saved_tensors
+            D = _internal.torch.birkhoff_proj_n4_backward(G, T)["D"]
+        return D.view(in_shape), None, None
 
 
 class MHCProjectionN4(nn.Module):
-    def __init__(self, tol=1e-6):
+    """save_duals=True (not in the reference) keeps R and the final duals
+    beta (16 bytes per matrix) for the backward instead of T (64), which then
+    rebuilds T bit for bit; gradients are identical."""
+
+    def __init__(self, tol=1e-6, save_duals=False):
         super().__init__()
         self.tol = tol
+        self.save_duals = save_duals
 
     def forward(self, x):
         in_shape = x.shape
         if x.ndim < 2 or in_shape[-1] != 4 or in_shape[-2] != 4:
             raise ValueError("x must be a tensor of size B x 4 x 4")
-        return MHCProjectionN4Function.apply(x, self.tol)
+        return MHCProjectionN4Function.apply(x, self.tol, self.save_duals)
 
 
 class MHCSinkhornN4Function(torch.autograd.Function):

@@ -121,3 +121,15 @@ def test_hres_noalloc_invalid_arguments_rejected(args):
     with pytest.raises(capi.MhcError) as e:
         capi.birkhoff_proj_n4_hres_backward_noalloc(*args)
     assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("fn,args", [
+    (capi.birkhoff_proj_n4_duals, (FAKE, FAKE, FAKE, 1e-6, -1)),
+    (capi.birkhoff_proj_n4_duals, (FAKE, FAKE, 0, 1e-6, 5)),
+    (capi.birkhoff_proj_n4_backward_duals, (FAKE, FAKE, 0, FAKE, 5)),
+    (capi.birkhoff_proj_n4_backward_duals, (FAKE, FAKE, FAKE, FAKE, -2)),
+])
+def test_duals_invalid_arguments_rejected(fn, args):
+    with pytest.raises(capi.MhcError) as e:
+        fn(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
