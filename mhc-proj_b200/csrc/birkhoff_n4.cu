@@ -12,6 +12,7 @@ constexpr int kNewtonBlock = 128;
 // kRing slots, kRingHalf at a time (8 KB per warp, 32 KB per block).
 constexpr int kRingHalf = 64;
 constexpr int kRing = 2 * kRingHalf;
+
 constexpr int kBackwardBlock = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -152,6 +153,12 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
     __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4];
+    // The line-search steps gamma_k as a per-warp table: one shared load per
+    // step instead of a chain of compares and selects.
+    __shared__ float gtab_all[kNewtonBlock / 32][8];
+    float* gtab = gtab_all[threadIdx.x >> 5];
+    if (lane < 8) gtab[lane] = line_step(lane);
+    __syncwarp();
     float4* ring = ring_all[threadIdx.x >> 5];
     auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
 #pragma unroll
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             fresh = false;
         }
         const bool col = s_alpha0 || s_skcol;
-        const float gamma = line_step(k);
+        const float gamma = gtab[k];
         // Point of evaluation (rows) or per-row offsets (columns).  -0 is the
         // offset of the alpha = 0 pass: x + (-0) == x for every x, so that pass
         // sees R itself, as in the reference.
@@ -282,8 +289,14 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
                 sel(reject_last, static_cast<int>(kSkCol),
                 sel(s_skcol, static_cast<int>(kSkEval), stage))))));
 
-        // T leaves with the pass that produced it.
-        if (s_eval0 || (done && !col)) store_elems<Elem, kVec>(Tout, static_cast<int64_t>(idx) * 16, Tn);
+        // T leaves with the pass that produced it: a predicated store (fp32,
+        // 16-byte aligned), so that no branch splits the warp here.
+        const bool store_t = s_eval0 || (done && !col);
+        if constexpr (kVec && sizeof(Elem) == 4) {
+            store_mat_if(store_t, reinterpret_cast<float*>(Tout) + static_cast<int64_t>(idx) * 16, Tn);
+        } else {
+            if (store_t) store_elems<Elem, kVec>(Tout, static_cast<int64_t>(idx) * 16, Tn);
+        }
         if constexpr (kStats) {
             if (done) {
                 iters_out[idx] = it;

@@ -55,6 +55,19 @@ __device__ __forceinline__ void store_mat(float* __restrict__ base, int64_t idx,
     }
 }
 
+// Four 128-bit streaming stores of a at p (16-byte aligned) when `pred`, as
+// predicated instructions rather than a branch around them.
+__device__ __forceinline__ void store_mat_if(bool pred, float* p, const Mat4& a)
+{
+    const unsigned on = pred ? 1u : 0u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        asm volatile("{ .reg .pred p; setp.ne.u32 p, %0, 0; @p st.global.cs.v4.f32 [%1], {%2, %3, %4, %5}; }"
+                     ::"r"(on), "l"(p + 4 * q), "f"(a.m[4 * q]), "f"(a.m[4 * q + 1]), "f"(a.m[4 * q + 2]),
+                       "f"(a.m[4 * q + 3])
+                     : "memory");
+}
+
 // Sum of four values in the pairwise order (a + b) + (c + d).  Sixteen lanes
 // of a half-warp reducing with xor-butterfly shuffles (offsets 1,2 for rows,
 // 4,8 for columns) all end with this value, so a single thread that owns the
