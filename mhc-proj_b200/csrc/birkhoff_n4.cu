@@ -13,6 +13,7 @@ constexpr int kNewtonBlock = 128;
 constexpr int kRingHalf = 64;
 constexpr int kRing = 2 * kRingHalf;
 
+
 constexpr int kBackwardBlock = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -185,6 +186,18 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             r.m[4 * j + 3] = v.w;
         }
     };
+    // take(i) as predicated shared loads: r keeps its value where !get.
+    auto take_if = [&](bool get, int i) {
+        const unsigned on = get ? 1u : 0u;
+        const unsigned addr =
+            static_cast<unsigned>(__cvta_generic_to_shared(ring + ((i & (kRing - 1)) * 4)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            asm volatile("{ .reg .pred p; setp.ne.u32 p, %4, 0; @p ld.shared.v4.f32 {%0, %1, %2, %3}, [%5]; }"
+                         : "+f"(r.m[4 * j]), "+f"(r.m[4 * j + 1]), "+f"(r.m[4 * j + 2]), "+f"(r.m[4 * j + 3])
+                         : "r"(on), "r"(addr + 16u * j)
+                         : "memory");
+    };
     fill(0);
     fill(kRingHalf);
     __syncwarp();
@@ -311,13 +324,12 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);
         if (want) {
-            if (done) {
-                idx = next + __popc(want & ((1u << lane) - 1u));
-                if (idx < cnt) {
-                    take(idx);
-                    stage = kEval0;
-                }
-            }
+            // finished lanes take the next matrices in lane order, without a branch
+            const int cand = next + __popc(want & ((1u << lane) - 1u));
+            const bool get = done && cand < cnt;
+            idx = sel(done, cand, idx);
+            take_if(get, cand);
+            stage = sel(get, static_cast<int>(kEval0), stage);
             next = min(cnt, next + __popc(want));
             if (next > base + kRingHalf) {  // the older half is all handed out: stage the next one
                 __syncwarp();
