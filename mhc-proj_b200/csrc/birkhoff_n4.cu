@@ -71,13 +71,16 @@ struct HResSource {
     }
 };
 
-// Four floats at p (16-byte aligned when kVec).
+// Four floats at p (16-byte aligned when kVec) when `pred`; a predicated
+// store on the 16-byte path.
 template <bool kVec>
-__device__ __forceinline__ void store_vec4(float* p, const float (&v)[4])
+__device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (&v)[4])
 {
     if constexpr (kVec) {
-        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    } else {
+        asm volatile("{ .reg .pred q; setp.ne.u32 q, %0, 0; @q st.global.v4.f32 [%1], {%2, %3, %4, %5}; }"
+                     ::"r"(pred ? 1u : 0u), "l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3])
+                     : "memory");
+    } else if (pred) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) p[j] = v[j];
     }
@@ -302,14 +305,9 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
                 sel(reject_last, static_cast<int>(kSkCol),
                 sel(s_skcol, static_cast<int>(kSkEval), stage))))));
 
-        // T leaves with the pass that produced it: a predicated store (fp32,
-        // 16-byte aligned), so that no branch splits the warp here.
-        const bool store_t = s_eval0 || (done && !col);
-        if constexpr (kVec && sizeof(Elem) == 4) {
-            store_mat_if(store_t, reinterpret_cast<float*>(Tout) + static_cast<int64_t>(idx) * 16, Tn);
-        } else {
-            if (store_t) store_elems<Elem, kVec>(Tout, static_cast<int64_t>(idx) * 16, Tn);
-        }
+        // T leaves with the pass that produced it: predicated stores on the
+        // 16-byte path, so that no branch splits the warp here.
+        store_elems_if<Elem, kVec>(s_eval0 || (done && !col), Tout, static_cast<int64_t>(idx) * 16, Tn);
         if constexpr (kStats) {
             if (done) {
                 iters_out[idx] = it;
@@ -319,7 +317,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         if constexpr (kDuals) {
             // beta of the output's point: the adopted one (an exit after a
             // column pass keeps the beta = 0 of the evaluation that wrote T)
-            if (done) store_vec4<kVec>(beta_out + static_cast<int64_t>(idx) * 4, beta);
+            store_vec4_if<kVec>(done, beta_out + static_cast<int64_t>(idx) * 4, beta);
         }
         // Hand finished lanes the warp's next matrices.
         const unsigned want = __ballot_sync(kFullMask, done);

@@ -165,6 +165,30 @@ __device__ __forceinline__ void store_elems(Elem* __restrict__ base, int64_t off
     }
 }
 
+// store_elems when `pred`: predicated 128-bit stores for the 16-byte path
+// (no branch), a branch around the scalar path.
+template <class Elem, bool kVec>
+__device__ __forceinline__ void store_elems_if(bool pred, Elem* __restrict__ base, int64_t off, const Mat4& a)
+{
+    if constexpr (kVec && sizeof(Elem) == 4) {
+        store_mat_if(pred, reinterpret_cast<float*>(base) + off, a);
+    } else if constexpr (kVec) {
+        const unsigned on = pred ? 1u : 0u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint4 v;
+            Elem* e = reinterpret_cast<Elem*>(&v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) e[k] = from_f32<Elem>(a.m[8 * h + k]);
+            asm volatile("{ .reg .pred p; setp.ne.u32 p, %0, 0; @p st.global.cs.v4.b32 [%1], {%2, %3, %4, %5}; }"
+                         ::"r"(on), "l"(base + off + 8 * h), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                         : "memory");
+        }
+    } else {
+        if (pred) store_elems<Elem, kVec>(base, off, a);
+    }
+}
+
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
