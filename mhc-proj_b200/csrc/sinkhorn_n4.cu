@@ -18,6 +18,10 @@ namespace mhcp {
 
 constexpr float kSkEps = 1e-8f;  // src/sinkhorn_knopp_n4.cu:10,18
 constexpr int kSkBlock = 128;
+// The backward replays the forward with the hardware reciprocal (sk_inv_approx):
+// its gradient must be that of the forward within tolerance, not bitwise, and
+// the correctly rounded reciprocal is most of the replay's cost.
+constexpr bool kSkBwdApprox = true;
 
 // exp of every entry (the fused kernels' input is the logits R).
 __device__ __forceinline__ void exp_inplace(Mat4& x)
@@ -105,7 +109,7 @@ __device__ __forceinline__ void sk_checkpoint(Pairs x, float2 (*ckpt)[8][kSkBloc
         for (int q = 0; q < 8; ++q) ckpt[s][q][tid] = x.p[q];
         if (s + 1 < kNumSeg) {
 #pragma unroll
-            for (int k = 0; k < kSkSeg; ++k) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
+            for (int k = 0; k < kSkSeg; ++k) sk_iteration<kSkBwdApprox>(x, kSkEps, nullptr, nullptr, nullptr);
         }
     }
 }
@@ -123,7 +127,7 @@ __device__ __forceinline__ void sk_reverse(Pairs& dy, float2 (*ckpt)[8][kSkBlock
         for (int q = 0; q < 8; ++q) x.p[q] = ckpt[s][q][tid];
 #pragma unroll
         for (int k = 0; k < kSkSeg; ++k)
-            if (k < len) sk_iteration(x, kSkEps, &xr[k], ri[k], ci[k]);
+            if (k < len) sk_iteration<kSkBwdApprox>(x, kSkEps, &xr[k], ri[k], ci[k]);
 #pragma unroll
         for (int k = kSkSeg - 1; k >= 0; --k)
             if (k < len) sk_iteration_vjp(dy, xr[k], ri[k], ci[k]);

@@ -28,6 +28,16 @@ constexpr int kSkSeg = 4;
 
 __device__ __forceinline__ float sk_inv(float s, float eps) { return (s > eps) ? __frcp_rn(s) : 0.0f; }
 
+// The same factor from the hardware reciprocal (rcp.approx.ftz: at most one
+// ulp from 1/s, against the half ulp of __frcp_rn) -- for the backward's
+// replay of the forward, which must be close to the forward, not equal to it.
+__device__ __forceinline__ float sk_inv_approx(float s, float eps)
+{
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+    return (s > eps) ? r : 0.0f;
+}
+
 // A matrix as eight float2 pairs, two per row: P[2i] = (x_i0, x_i1),
 // P[2i+1] = (x_i2, x_i3).  Column-wise work then runs on packed fp32x2
 // arithmetic (two IEEE round-to-nearest operations per instruction on
@@ -65,14 +75,16 @@ __device__ __forceinline__ Mat4 from_pairs(const Pairs& r)
 // the column scaling, so their multiplies are not contracted into the column
 // sums); with the correctly rounded reciprocal the result is the reference's
 // bit for bit.
+template <bool kApprox = false>
 __device__ __forceinline__ void sk_iteration(Pairs& x, float eps, Pairs* xr_out, float* rinv_out,
                                              float* cinv_out)
 {
+    auto inv = [eps](float v) { return kApprox ? sk_inv_approx(v, eps) : sk_inv(v, eps); };
     float ri[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const float2 a = x.p[2 * i], b = x.p[2 * i + 1];
-        ri[i] = sk_inv(__fadd_rn(__fadd_rn(__fadd_rn(a.x, a.y), b.x), b.y), eps);
+        ri[i] = inv(__fadd_rn(__fadd_rn(__fadd_rn(a.x, a.y), b.x), b.y));
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -83,8 +95,8 @@ __device__ __forceinline__ void sk_iteration(Pairs& x, float eps, Pairs* xr_out,
     // column sums ((x_0j + x_1j) + x_2j) + x_3j, two columns per instruction
     const float2 c01 = __fadd2_rn(__fadd2_rn(__fadd2_rn(x.p[0], x.p[2]), x.p[4]), x.p[6]);
     const float2 c23 = __fadd2_rn(__fadd2_rn(__fadd2_rn(x.p[1], x.p[3]), x.p[5]), x.p[7]);
-    const float2 ci01 = make_float2(sk_inv(c01.x, eps), sk_inv(c01.y, eps));
-    const float2 ci23 = make_float2(sk_inv(c23.x, eps), sk_inv(c23.y, eps));
+    const float2 ci01 = make_float2(inv(c01.x), inv(c01.y));
+    const float2 ci23 = make_float2(inv(c23.x), inv(c23.y));
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         x.p[2 * i] = __fmul2_rn(x.p[2 * i], ci01);

@@ -180,12 +180,17 @@ def test_sinkhorn_pair_matches_vanilla_autograd():
 
 @pytest.mark.parametrize("iters", [1, 2, 3, 4, 5, 9, 16, 19, 20])
 def test_sinkhorn_backward_every_iteration_count(iters):
+    """The exact VJP for every iteration count: against the oracle's (which
+    replays the forward with correctly rounded reciprocals) within 2e-6,
+    relative where |dM| > 1 -- the kernel's replay uses the hardware
+    reciprocal (one ulp), and dM = dR / M grows where M is small -- and dR
+    within 1e-5 of vanilla autograd."""
     n = 4096
     M = torch.exp(make_logits("normal", n, seed=iters))
     G = make_logits("normal", n, seed=iters + 50)
     D = capi.sinkhorn_knopp_n4_backward_tensor(G, M, iters)
     Do = oracle.sinkhorn_knopp_n4_backward(G.cpu().numpy(), M.cpu().numpy(), iters, 1e-8, exact=True)
-    assert np.max(np.abs(D.cpu().numpy() - Do)) < 2e-6
+    assert (np.abs(D.cpu().numpy() - Do) <= 2e-6 * np.maximum(1.0, np.abs(Do))).all()
     x = torch.log(M)
     _, dRv = oracle.vanilla_sinkhorn(x, G, iters=iters)
     assert (D * M - dRv).abs().max().item() < TOL
