@@ -56,15 +56,13 @@ struct HResSource {
     const float* rms;
     const float* alpha;
     const float* b;
-    __device__ __forceinline__ void advance(int64_t k)
-    {
-        h += k * stride;
-        rms += k;
-    }
+    int64_t base = 0;  // the warp's first matrix: one live index instead of two moved pointers
+    __device__ __forceinline__ void advance(int64_t k) { base = k; }
     __device__ __forceinline__ void load(int i, Mat4& r) const
     {
-        load_elems<float, kVec>(h, static_cast<int64_t>(i) * stride, r);
-        const float rinv = hres_rinv(__ldg(rms + i));
+        const int64_t k = base + i;
+        load_elems<float, kVec>(h, k * stride, r);
+        const float rinv = hres_rinv(__ldg(rms + k));
         const float a = __ldg(alpha);
 #pragma unroll
         for (int e = 0; e < 16; ++e) r.m[e] = hres_logit(a, r.m[e], rinv, __ldg(b + e));
