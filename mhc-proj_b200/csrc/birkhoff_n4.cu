@@ -94,9 +94,11 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // Every step is the same straight-line code for every lane: the Newton
 // direction at the lane's current point, one log-sum-exp pass whose lines are
 // rows or columns as the stage needs, the row and the column
-// post-processing, and the transition, all as selects.  No branch depends on
-// a lane's stage, so lanes at different points of the algorithm never split
-// the warp; the only branches are the warp-wide refill and the stores.
+// post-processing, and the transition, all as selects; the store of a
+// finished T and the refill of its lane are predicated instructions.  No
+// branch depends on a lane, so lanes at different points of the algorithm
+// never split the warp; the only branches are warp-uniform (the loop, the
+// refill when some lane finished, the ring's fill).
 //
 // The current point keeps only what the next direction needs -- the column
 // sums, the six Gram sums of T, f and |g| -- not T itself: T is written to
@@ -107,8 +109,8 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // The warp's next matrices wait in a shared-memory ring: all 32 lanes load
 // (and, for HResSource, transform) kRingHalf matrices at once whenever the
 // older half of the ring has been handed out, so that a refill -- which a
-// few lanes of the warp take each step -- is four shared-memory loads
-// instead of global loads and arithmetic issued for those few lanes alone.
+// few lanes of the warp take each step -- is four predicated shared-memory
+// loads instead of global loads and arithmetic issued for those few lanes.
 // The bound of 5 blocks per SM keeps the register count at the 5-block
 // occupancy (96 registers) that the ring's addressing would otherwise push
 // past.
