@@ -14,6 +14,7 @@ constexpr int kRingHalf = 64;
 constexpr int kRing = 2 * kRingHalf;
 
 
+
 constexpr int kBackwardBlock = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
 
@@ -234,12 +235,13 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         // offset of the alpha = 0 pass: x + (-0) == x for every x, so that pass
         // sees R itself, as in the reference.
         float v[4];
+        const float zero = sel(s_eval0, 0.0f, -0.0f);
+        const bool s_zero = s_eval0 || s_alpha0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const float base = sel(s_skcol, alpha[j], beta[j]);
             const float cand = __fmaf_rn(gamma, d[j], beta[j]);
-            const float vj = sel(s_cand, cand, base);
-            v[j] = sel(s_eval0, 0.0f, sel(s_alpha0, -0.0f, vj));
+            v[j] = sel(s_zero, zero, sel(s_cand, cand, base));
         }
         float X[16];
 #pragma unroll
@@ -319,22 +321,20 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             // column pass keeps the beta = 0 of the evaluation that wrote T)
             store_vec4_if<kVec>(done, beta_out + static_cast<int64_t>(idx) * 4, beta);
         }
-        // Hand finished lanes the warp's next matrices.
+        // Finished lanes take the warp's next matrices in lane order.  No
+        // branch, not even on `want`: with no finished lane nothing changes.
         const unsigned want = __ballot_sync(kFullMask, done);
-        if (want) {
-            // finished lanes take the next matrices in lane order, without a branch
-            const int cand = next + __popc(want & ((1u << lane) - 1u));
-            const bool get = done && cand < cnt;
-            idx = sel(done, cand, idx);
-            take_if(get, cand);
-            stage = sel(get, static_cast<int>(kEval0), stage);
-            next = min(cnt, next + __popc(want));
-            if (next > base + kRingHalf) {  // the older half is all handed out: stage the next one
-                __syncwarp();
-                fill(base + kRing);
-                __syncwarp();
-                base += kRingHalf;
-            }
+        const int cand = next + __popc(want & ((1u << lane) - 1u));
+        const bool get = done && cand < cnt;
+        idx = sel(done, cand, idx);
+        take_if(get, cand);
+        stage = sel(get, static_cast<int>(kEval0), stage);
+        next = min(cnt, next + __popc(want));
+        if (next > base + kRingHalf) {  // the older half is all handed out: stage the next one
+            __syncwarp();
+            fill(base + kRing);
+            __syncwarp();
+            base += kRingHalf;
         }
     }
 }
