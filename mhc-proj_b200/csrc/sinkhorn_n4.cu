@@ -23,6 +23,7 @@ constexpr int kSkBlock = 128;
 // the correctly rounded reciprocal is most of the replay's cost.
 constexpr bool kSkBwdApprox = true;
 
+
 // exp of every entry (the fused kernels' input is the logits R).
 __device__ __forceinline__ void exp_inplace(Mat4& x)
 {
@@ -103,7 +104,10 @@ template <int kIters>
 __device__ __forceinline__ void sk_checkpoint(Pairs x, float2 (*ckpt)[8][kSkBlock], int tid)
 {
     constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-#pragma unroll
+    // Segments are not unrolled: the 20-iteration body unrolled five times
+    // overflowed the instruction cache (instruction-fetch stalls first) and
+    // needed 167 registers instead of 122.
+#pragma unroll 1
     for (int s = 0; s < kNumSeg; ++s) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) ckpt[s][q][tid] = x.p[q];
@@ -118,7 +122,7 @@ template <int kIters>
 __device__ __forceinline__ void sk_reverse(Pairs& dy, float2 (*ckpt)[8][kSkBlock], int tid)
 {
     constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-#pragma unroll
+#pragma unroll 1
     for (int s = kNumSeg - 1; s >= 0; --s) {
         const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kSkSeg;
         Pairs x, xr[kSkSeg];

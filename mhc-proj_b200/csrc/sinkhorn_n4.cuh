@@ -26,6 +26,7 @@ namespace mhcp {
 constexpr int kSkMaxIters = 20;  // the reference's backward limit, sinkhorn_knopp.cuh:1213
 constexpr int kSkSeg = 4;
 
+
 // The correctly rounded reciprocal (round to nearest even, flush-to-zero) from
 // the hardware approximation and one Newton step on a fused multiply-add, the
 // correction of P. Markstein ("Computation of elementary functions on the IBM
