@@ -183,17 +183,24 @@ MHC_API int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float* d_
                                                void* d_workspace, int64_t workspace_bytes,
                                                cudaStream_t stream);
 
-/* mhc_birkhoff_proj_n4_hres_backward without a caller workspace and with no
- * allocation of any kind: the partial sums go to a fixed 68 KB array in the
- * library's device memory (1024 rows of 17 floats; the call uses at most
- * 1024 blocks, so every N fits), whose address is looked up once per device
- * on the first call there.  Same results as the workspace form given the
- * size that mhc_birkhoff_proj_n4_hres_backward_workspace reports (on a GPU
- * whose resident-block wave is at most 1024 blocks, B200 included).  The
- * array is shared by every call on a device: calls whose kernels may overlap
- * on the GPU (different streams without ordering) race and must not be
- * issued.  Nothing in it has to start at zero: each call writes every row it
- * reads first.  No reference counterpart. */
+/* mhc_birkhoff_proj_n4_hres_backward for callers that cannot allocate device
+ * memory: code running under a framework or serving engine that has already
+ * claimed the device's memory as its own pool and hands this library no
+ * allocator, and latency-bound loops that cannot afford cudaMalloc/cudaFree,
+ * which can synchronise the whole device.  It takes no workspace and
+ * allocates nothing: the per-block partial sums go to a fixed 68 KB array
+ * that is part of the library (1024 rows of 17 floats), which every GPU that
+ * loads the library holds until the process exits.  The call uses at most
+ * 1024 blocks, one row each, so no batch size needs more than the array.
+ * The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) and keeps it; make that first call before any stream
+ * capture.  Same results as the workspace form given the size that
+ * mhc_birkhoff_proj_n4_hres_backward_workspace reports (on a GPU whose
+ * resident-block wave is at most 1024 blocks, B200 included).  The array is
+ * shared by every call on a device and keeps the last call's sums: calls
+ * whose kernels may overlap on the GPU (different streams without ordering)
+ * race and must not be issued.  Nothing in it has to start at zero: each call
+ * writes every row it reads first.  No counterpart in the reference. */
 MHC_API int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, const float* d_T,
                                                        const float* d_h, int64_t h_stride,
                                                        const float* d_rms, const float* d_alpha,

@@ -556,26 +556,36 @@ static int hres_backward_launch(const float* G, const float* T, const float* h, 
     return static_cast<int>(cudaGetLastError());
 }
 
-// Scratch of mhc_birkhoff_proj_n4_hres_backward_noalloc: partial sums for up
-// to kNoAllocRows blocks (68 KB), in the library's own device memory.  Every
-// call writes each row it reads before reading it, so nothing in it has to
-// start at zero; calls whose kernels overlap on the GPU share it and race.
+// Scratch of mhc_birkhoff_proj_n4_hres_backward_noalloc, for callers that
+// cannot allocate device memory: partial sums for up to kNoAllocRows blocks
+// (68 KB), part of the library's own image, so every GPU that loads the
+// library holds it until the process exits.  Every call writes each row it
+// reads before reading it, so nothing in it has to start at zero; calls
+// whose kernels overlap on the GPU share it and race.
 constexpr int kNoAllocRows = 1024;
 static __device__ __align__(256) float g_hres_partials[kNoAllocRows * kHResPartials];
 
-// Address of g_hres_partials on the current device, looked up once per device.
-static float* noalloc_partials()
+// Device address of g_hres_partials on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up
+// (cudaGetSymbolAddress, with the device current) on the first call on each
+// device and kept; the lookup's status is returned as is.
+static cudaError_t noalloc_partials(float** out)
 {
     static std::atomic<float*> cache[kMaxDevices];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     float* p = cache[dev].load(std::memory_order_acquire);
-    if (p) return p;
-    void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, g_hres_partials) != cudaSuccess) return nullptr;
-    p = static_cast<float*>(addr);
-    cache[dev].store(p, std::memory_order_release);
-    return p;
+    if (!p) {
+        void* addr = nullptr;
+        e = cudaGetSymbolAddress(&addr, g_hres_partials);
+        if (e != cudaSuccess) return e;
+        p = static_cast<float*>(addr);
+        cache[dev].store(p, std::memory_order_release);
+    }
+    *out = p;
+    return cudaSuccess;
 }
 
 static bool valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
@@ -690,8 +700,12 @@ extern "C" int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, cons
     if (N < 0 || h_stride < 0 || dh_stride < 0 || !d_dalpha || !d_db ||
         (N > 0 && (!d_G || !d_T || !d_h || !d_rms || !d_alpha || !d_dh || !d_drms)))
         return MHC_ERR_INVALID_VALUE;
-    float* partials = noalloc_partials();
-    const int blocks = partials ? hres_backward_blocks(N, kNoAllocRows) : -1;
+    float* partials = nullptr;
+    const cudaError_t se = noalloc_partials(&partials);
+    if (se != cudaSuccess) return static_cast<int>(se);
+    // at most kNoAllocRows blocks, each row of the array one block's sums:
+    // no batch size needs more scratch than the array holds
+    const int blocks = hres_backward_blocks(N, kNoAllocRows);
     if (blocks < 0) {
         const cudaError_t e = cudaGetLastError();
         return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);

@@ -1,11 +1,16 @@
 """The no-allocation form of the fused H_res backward
-(mhc_birkhoff_proj_n4_hres_backward_noalloc), which keeps its partial sums in
-a fixed array of the library's device memory instead of a caller workspace.
+(mhc_birkhoff_proj_n4_hres_backward_noalloc), for callers that cannot
+allocate device memory -- a framework or serving engine that owns the
+device's memory pool, or a loop that cannot afford cudaMalloc/cudaFree
+synchronising the device.  It keeps its partial sums in a fixed array inside
+the library instead of a caller workspace.
 
-Collected last on purpose (the file name), so that it runs both after every
-other GPU test and on its own: two calls in a row, on different batches and
-sizes, each give the bits of the workspace entry point on the same inputs --
-the fixed array needs no reset between calls."""
+Collected last on purpose (the file name), so that a run that stops at the
+first failure has run every other test before it; it also passes on its own
+in a fresh process.  Two calls in a row, on different batches and sizes, each
+give the bits of the workspace entry point on the same inputs (the tests'
+tolerance for this backward is bitwise) -- the fixed array needs no reset
+between calls."""
 import pytest
 import torch
 
