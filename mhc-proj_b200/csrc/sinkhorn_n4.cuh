@@ -45,6 +45,9 @@ __device__ __forceinline__ float rcp_rn(float x)
     return (e != e) ? r0 : r1;
 }
 
+// The Sinkhorn-Knopp factor: s > eps ? 1/s : 0 with the reciprocal correctly
+// rounded.  Equal to (s > eps) ? __frcp_rn(s) : 0 for all 2^32 s at eps = 1e-8
+// (tests/test_reciprocal_gpu.py).
 __device__ __forceinline__ float sk_inv(float s, float eps) { return (s > eps) ? rcp_rn(s) : 0.0f; }
 
 // The same factor from the hardware reciprocal (rcp.approx.ftz: at most one

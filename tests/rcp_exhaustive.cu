@@ -1,6 +1,7 @@
 // Test infrastructure: compares mhcp::rcp_rn (sinkhorn_n4.cuh) with CUDA's
-// __frcp_rn on all 2^32 float bit patterns, both with flush-to-zero (built
-// with the Sinkhorn-Knopp kernels' flags).  Prints the number of inputs whose
+// __frcp_rn, and the Sinkhorn-Knopp factor mhcp::sk_inv(s, 1e-8) with
+// (s > 1e-8 ? __frcp_rn(s) : 0), on all 2^32 float bit patterns, all with
+// flush-to-zero (built with the Sinkhorn-Knopp kernels' flags).  Prints the number of inputs whose
 // results differ in any bit and exits 0.
 #include <cstdint>
 #include <cstdio>
@@ -14,7 +15,9 @@ __global__ void compare_all(unsigned long long* count, unsigned* first)
     unsigned long long local = 0;
     for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < (1ull << 32); i += step) {
         const float x = __uint_as_float(static_cast<unsigned>(i));
-        if (__float_as_uint(__frcp_rn(x)) != __float_as_uint(mhcp::rcp_rn(x))) {
+        const float want_inv = (x > 1e-8f) ? __frcp_rn(x) : 0.0f;
+        if (__float_as_uint(__frcp_rn(x)) != __float_as_uint(mhcp::rcp_rn(x)) ||
+            __float_as_uint(want_inv) != __float_as_uint(mhcp::sk_inv(x, 1e-8f))) {
             ++local;
             const unsigned slot = atomicAdd(first, 1u);
             if (slot < 8) first[1 + slot] = static_cast<unsigned>(i);

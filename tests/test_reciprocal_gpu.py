@@ -1,8 +1,10 @@
 """The Sinkhorn-Knopp kernels' reciprocal (rcp_rn in sinkhorn_n4.cuh: the
 hardware approximation plus one Newton step on a fused multiply-add) is the
 correctly rounded reciprocal: equal to CUDA's __frcp_rn on every one of the
-2^32 float inputs, bit for bit, with the kernels' flush-to-zero.  The check
-is a small CUDA program built here against the shipped header."""
+2^32 float inputs, bit for bit, with the kernels' flush-to-zero; and the
+kernels' factor sk_inv(s, 1e-8) equals (s > 1e-8 ? __frcp_rn(s) : 0) on all of
+them.  The check is a small CUDA program built here against the shipped
+header."""
 import os
 import shutil
 import subprocess
