@@ -85,3 +85,24 @@ def test_empty_batch_writes_zero_sums():
                                                 db.data_ptr(), 0, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert float(dalpha) == 0.0 and bool((db == 0).all())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_each_device_uses_its_own_array():
+    """The array is looked up on the first call on each device: a call on the
+    second GPU, right after one on the first, still matches the workspace
+    form there, and the first GPU's results stay right afterwards."""
+    first = inputs(50001, 3)
+    got0 = without_allocation(*first)
+    with torch.cuda.device(1):
+        second = inputs(60007, 4)
+        got1 = without_allocation(*second)
+        want1 = with_workspace(*second)
+        torch.cuda.synchronize()
+        for g, w in zip(got1, want1):
+            assert same_bits(g, w)
+    want0 = with_workspace(*first)
+    again0 = without_allocation(*first)
+    torch.cuda.synchronize()
+    for g, a, w in zip(got0, again0, want0):
+        assert same_bits(g, w) and same_bits(a, w)
