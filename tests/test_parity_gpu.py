@@ -286,3 +286,32 @@ def test_batch_beyond_int32_element_indexing():
         assert bitwise_equal(D[a:b], capi.birkhoff_proj_n4_backward_tensor(G[a:b].contiguous(), Ts))
     del R, G, T, D
     torch.cuda.empty_cache()
+
+
+def test_multi_gpu_workload_at_full_size(ref):
+    """The multi-GPU workload's whole batch on one GPU: N = 2^26 matrices of the
+    mixture (50% N(0,1), 25% N(0,9), 25% N(0,1) with +6 on one entry per row),
+    tol 1e-6, G ~ N(0,1): T and D equal the reference kernels' bit for bit,
+    and every row of T sums to 1 within 1e-5."""
+    n = 1 << 26
+    free, _ = torch.cuda.mem_get_info()
+    if free < 7 * n * 64:
+        pytest.skip("needs ~30 GB of free device memory")
+    R = torch.empty(n, 4, 4, device="cuda")
+    G = torch.empty(n, 4, 4, device="cuda")
+    for i in range(0, n, 1 << 24):
+        R[i:i + (1 << 24)] = make_logits("mixture", 1 << 24, seed=500 + i // (1 << 24))
+        G[i:i + (1 << 24)] = make_logits("normal", 1 << 24, seed=600 + i // (1 << 24))
+    T = capi.birkhoff_proj_n4_tensor(R)
+    Tr = ref_forward(ref, R)
+    torch.cuda.synchronize()
+    assert bitwise_equal(T, Tr)
+    del Tr
+    D = capi.birkhoff_proj_n4_backward_tensor(G, T)
+    Dr = ref_backward(ref, G, T)
+    torch.cuda.synchronize()
+    assert bitwise_equal(D, Dr)
+    del Dr, D, G
+    assert float((T.sum(2) - 1.0).abs().max()) < TOL
+    del R, T
+    torch.cuda.empty_cache()
