@@ -8,8 +8,8 @@ reference's own CUDA kernels compiled unmodified from their source files,
 src/utils.cuh, ``ref_hres_shim.cu``).
 
 Only the tests, the smoke check and the CPU-baseline leg of the benchmark use
-this package, always as the checker or the timed baseline, never as a product
-path.  Build both libraries with ``make -C oracle``.
+this package, always as the oracle the kernels are compared with or as the timed
+baseline, never as a product path.  Build both libraries with ``make -C oracle``.
 """
 from __future__ import annotations
 

@@ -2,8 +2,8 @@
  * ORACLE -- test infrastructure only.
  *
  * CPU restatement of the reference mHC-proj algorithms for the batched n=4
- * Birkhoff projection.  It is the checker for the CUDA kernels of this
- * repository and the timed CPU baseline; no product code path calls it.
+ * Birkhoff projection.  It is the oracle the CUDA kernels of this repository
+ * are compared with, and the timed CPU baseline; no product code path calls it.
  *
  * What it restates (file:line in the reference project):
  *   - the dual-Newton forward        src/birkhoff_proj_n4.cu:375-499
