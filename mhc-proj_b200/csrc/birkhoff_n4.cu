@@ -143,7 +143,6 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         iters_out += begin;
         gnorm_out += begin;
     }
-    if constexpr (kDuals) beta_out += begin * 4;
 
     Mat4 r;                 // logits of the lane's matrix
     float p[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // Gram sums of T at the current point
@@ -157,7 +156,9 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     bool fresh = false;     // a new Newton iteration starts: take the direction now
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
-    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4];
+    // kDuals: one more 16-byte entry per warp after the ring holds the
+    // warp's beta pointer (below).
+    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4 + (kDuals ? 1 : 0)];
     // The line-search steps gamma_k as a per-warp table: one shared load per
     // step instead of a chain of compares and selects.
     __shared__ float gtab_all[kNewtonBlock / 32][8];
@@ -165,6 +166,13 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     if (lane < 8) gtab[lane] = line_step(lane);
     __syncwarp();
     float4* ring = ring_all[threadIdx.x >> 5];
+    // The warp's beta pointer lives in shared memory at a fixed offset from
+    // the ring, not in two registers: at the 96-register cap of 5 blocks per
+    // SM those two spilled (3.31 ms at 2^24 instead of 3.17).  The fills'
+    // __syncwarp below orders this store before every lane's load.
+    if constexpr (kDuals) {
+        if (lane == 0) *reinterpret_cast<float**>(ring + kRing * 4) = beta_out + begin * 4;
+    }
     auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
 #pragma unroll
         for (int u = 0; u < kRingHalf / 32; ++u) {
@@ -319,7 +327,10 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         if constexpr (kDuals) {
             // beta of the output's point: the adopted one (an exit after a
             // column pass keeps the beta = 0 of the evaluation that wrote T)
-            store_vec4_if<kVec>(done, beta_out + static_cast<int64_t>(idx) * 4, beta);
+            float* warp_beta;  // a volatile load, so that it is not hoisted into registers
+            asm volatile("ld.shared.u64 %0, [%1];" : "=l"(warp_beta)
+                         : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * 4))));
+            store_vec4_if<kVec>(done, warp_beta + static_cast<int64_t>(idx) * 4, beta);
         }
         // Finished lanes take the warp's next matrices in lane order.  No
         // branch, not even on `want`: with no finished lane nothing changes.
