@@ -156,9 +156,9 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     bool fresh = false;     // a new Newton iteration starts: take the direction now
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
-    // kDuals: one more 16-byte entry per warp after the ring holds the
-    // warp's beta pointer (below).
-    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4 + (kDuals ? 1 : 0)];
+    // One more 16-byte entry per warp after the ring holds the warp's output
+    // pointer (below).
+    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4 + 1];
     // The line-search steps gamma_k as a per-warp table: one shared load per
     // step instead of a chain of compares and selects.
     __shared__ float gtab_all[kNewtonBlock / 32][8];
@@ -166,13 +166,25 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     if (lane < 8) gtab[lane] = line_step(lane);
     __syncwarp();
     float4* ring = ring_all[threadIdx.x >> 5];
-    // The warp's beta pointer lives in shared memory at a fixed offset from
-    // the ring, not in two registers: at the 96-register cap of 5 blocks per
-    // SM those two spilled (3.31 ms at 2^24 instead of 3.17).  The fills'
+    // One output pointer of the warp lives in shared memory at a fixed offset
+    // from the ring instead of in two registers, and is loaded where it is
+    // stored through: beta's for kDuals (as two more registers it made that
+    // instantiation spill at the 96-register cap of 5 blocks per SM: 3.31 ms
+    // at 2^24 instead of 3.17), T's otherwise (3.08 -> 3.05 ms).  The fills'
     // __syncwarp below orders this store before every lane's load.
-    if constexpr (kDuals) {
-        if (lane == 0) *reinterpret_cast<float**>(ring + kRing * 4) = beta_out + begin * 4;
+    if (lane == 0) {
+        if constexpr (kDuals)
+            *reinterpret_cast<float**>(ring + kRing * 4) = beta_out + begin * 4;
+        else
+            *reinterpret_cast<Elem**>(ring + kRing * 4) = Tout;
     }
+    // The pointer, by a volatile load so that it is not hoisted into registers.
+    auto warp_pointer = [&]() {
+        unsigned long long v;
+        asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v)
+                     : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * 4))));
+        return v;
+    };
     auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
 #pragma unroll
         for (int u = 0; u < kRingHalf / 32; ++u) {
@@ -317,7 +329,9 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
 
         // T leaves with the pass that produced it: predicated stores on the
         // 16-byte path, so that no branch splits the warp here.
-        store_elems_if<Elem, kVec>(s_eval0 || (done && !col), Tout, static_cast<int64_t>(idx) * 16, Tn);
+        Elem* t_at = Tout;
+        if constexpr (!kDuals) t_at = reinterpret_cast<Elem*>(warp_pointer());
+        store_elems_if<Elem, kVec>(s_eval0 || (done && !col), t_at, static_cast<int64_t>(idx) * 16, Tn);
         if constexpr (kStats) {
             if (done) {
                 iters_out[idx] = it;
@@ -327,10 +341,8 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         if constexpr (kDuals) {
             // beta of the output's point: the adopted one (an exit after a
             // column pass keeps the beta = 0 of the evaluation that wrote T)
-            float* warp_beta;  // a volatile load, so that it is not hoisted into registers
-            asm volatile("ld.shared.u64 %0, [%1];" : "=l"(warp_beta)
-                         : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * 4))));
-            store_vec4_if<kVec>(done, warp_beta + static_cast<int64_t>(idx) * 4, beta);
+            store_vec4_if<kVec>(done, reinterpret_cast<float*>(warp_pointer()) + static_cast<int64_t>(idx) * 4,
+                                beta);
         }
         // Finished lanes take the warp's next matrices in lane order.  No
         // branch, not even on `want`: with no finished lane nothing changes.
