@@ -10,7 +10,7 @@ namespace mhcp {
 constexpr int kNewtonBlock = 128;
 // Each forward warp stages its next matrices in a shared-memory ring of
 // kRing slots, kRingHalf at a time (8 KB per warp, 32 KB per block).
-constexpr int kRingHalf = 64;
+constexpr int kRingHalf = 32;
 constexpr int kRing = 2 * kRingHalf;
 
 
@@ -19,14 +19,16 @@ constexpr int kBackwardBlock = 256;
 constexpr unsigned kFullMask = 0xffffffffu;
 
 // Stages of the per-lane state machine.  Each stage is one log-sum-exp pass.
+// The two passes that depend on R alone -- the objective at beta = 0
+// (birkhoff_proj_n4.cu:402-409) and the alpha = 0 initialisation (:414-415)
+// -- are made when the matrix is staged (`start_point`), so a lane starts at
+// the better of the two points.
 enum Stage : int {
-    kEval0 = 0,   // f/gradient at beta = 0                           (birkhoff_proj_n4.cu:402-409)
-    kAlpha0 = 1,  // column LSE of R: the alpha = 0 initialisation    (:414-415)
-    kEvalA = 2,   // f/gradient at the alpha = 0 beta, if it is better (:416-423)
-    kCand = 3,    // line-search candidate beta + gamma_k d           (:450-477)
-    kSkCol = 4,   // column half of the Sinkhorn fallback sweep       (:480-482)
-    kSkEval = 5,  // f/gradient after the sweep                        (:483-486)
-    kIdle = 6,
+    kStart = 0,   // f/gradient at the starting point, then the first convergence test (:416-431)
+    kCand = 1,    // line-search candidate beta + gamma_k d           (:450-477)
+    kSkCol = 2,   // column half of the Sinkhorn fallback sweep       (:480-482)
+    kSkEval = 3,  // f/gradient after the sweep                        (:483-486)
+    kIdle = 4,
 };
 
 // Where the forward finds matrix k's logits.  `advance` moves to a warp's
@@ -92,29 +94,31 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // over 32 instead of the maximum over each group of 32 (per-matrix work ranges
 // from 4 to ~140 evaluations).
 //
-// Every step is the same straight-line code for every lane: the Newton
-// direction at the lane's current point, one log-sum-exp pass whose lines are
-// rows or columns as the stage needs, the row and the column
-// post-processing, and the transition, all as selects; the store of a
-// finished T and the refill of its lane are predicated instructions.  No
-// branch depends on a lane, so lanes at different points of the algorithm
-// never split the warp; the only branches are warp-uniform (the loop, the
-// refill when some lane finished, the ring's fill).
+// Every step is the same straight-line code for every lane: one log-sum-exp
+// pass whose lines are rows or columns as the stage needs, the row and the
+// column post-processing, the transition, and the Newton direction at the
+// point just evaluated (kept by the lanes that adopt that point and start a
+// new iteration), all as selects; the store of a finished T and the refill
+// of its lane are predicated instructions.  No branch depends on a lane, so
+// lanes at different points of the algorithm never split the warp; the only
+// branches are warp-uniform (the loop, the ring's fill).
 //
-// The current point keeps only what the next direction needs -- the column
-// sums, the six Gram sums of T, f and |g| -- not T itself: T is written to
-// the output by the pass that finishes the matrix.  The beta = 0 evaluation
-// writes its T as well, for the one exit that comes after a column pass (the
-// alpha = 0 initialisation rejected and beta = 0 already converged).
+// The current point keeps only f, |g|, the row log-sum-exps (the offsets of
+// a Sinkhorn sweep) and beta -- not T, whose column and Gram sums give the
+// direction in the step that evaluates it: T is written to the output by the
+// pass that finishes the matrix.
 //
 // The warp's next matrices wait in a shared-memory ring: all 32 lanes load
 // (and, for HResSource, transform) kRingHalf matrices at once whenever the
-// older half of the ring has been handed out, so that a refill -- which a
-// few lanes of the warp take each step -- is four predicated shared-memory
-// loads instead of global loads and arithmetic issued for those few lanes.
-// The bound of 5 blocks per SM keeps the register count at the 5-block
-// occupancy (96 registers) that the ring's addressing would otherwise push
-// past.
+// older half of the ring has been handed out, and choose each one's starting
+// point there (`start_point`: the beta = 0 objective and the alpha = 0
+// initialisation, two passes that depend on R alone, made at full warp width
+// instead of as two steps of the state machine).  A refill -- which a few
+// lanes of the warp take each step -- is then five predicated shared-memory
+// loads (R and the starting beta) instead of global loads and arithmetic
+// issued for those few lanes.  The bound of 5 blocks per SM keeps the
+// register count at the 5-block occupancy (96 registers) that the ring's
+// addressing would otherwise push past.
 //
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
@@ -144,21 +148,20 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         gnorm_out += begin;
     }
 
-    Mat4 r;                 // logits of the lane's matrix
-    float p[6] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // Gram sums of T at the current point
-    float c[3] = {0.0f, 0.0f, 0.0f};  // column sums of T (the fourth is never used)
+    Mat4 r = {};            // logits of the lane's matrix
     float f = 0.0f;         // objective at the current point
     float gn = 0.0f;        // gradient l1 norm at the current point
     float alpha[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // row LSE at the current point
     float beta[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     int k = 0, it = 0;
-    bool fresh = false;     // a new Newton iteration starts: take the direction now
     int idx = lane;  // offset in the warp's slice
     int stage = kIdle;
-    // One more 16-byte entry per warp after the ring holds the warp's output
-    // pointer (below).
-    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * 4 + 1];
+    // A ring slot is five 16-byte entries: the four rows of R and the
+    // starting beta.  One more entry per warp after the ring holds the warp's
+    // output pointer (below).
+    constexpr int kSlot = 5;
+    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * kSlot + 1];
     // The line-search steps gamma_k as a per-warp table: one shared load per
     // step instead of a chain of compares and selects.
     __shared__ float gtab_all[kNewtonBlock / 32][8];
@@ -174,100 +177,78 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     // __syncwarp below orders this store before every lane's load.
     if (lane == 0) {
         if constexpr (kDuals)
-            *reinterpret_cast<float**>(ring + kRing * 4) = beta_out + begin * 4;
+            *reinterpret_cast<float**>(ring + kRing * kSlot) = beta_out + begin * 4;
         else
-            *reinterpret_cast<Elem**>(ring + kRing * 4) = Tout;
+            *reinterpret_cast<Elem**>(ring + kRing * kSlot) = Tout;
     }
     // The pointer, by a volatile load so that it is not hoisted into registers.
     auto warp_pointer = [&]() {
         unsigned long long v;
         asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v)
-                     : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * 4))));
+                     : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * kSlot))));
         return v;
     };
     auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
-#pragma unroll
+#pragma unroll 1
         for (int u = 0; u < kRingHalf / 32; ++u) {
             const int i = first + 32 * u + lane;
             if (i < cnt) {
                 Mat4 m;
                 src.load(i, m);
-                float4* slot = ring + (i & (kRing - 1)) * 4;
+                float b[4];
+                start_point(m.m, b);
+                float4* slot = ring + (i & (kRing - 1)) * kSlot;
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     slot[j] = make_float4(m.m[4 * j], m.m[4 * j + 1], m.m[4 * j + 2], m.m[4 * j + 3]);
+                slot[4] = make_float4(b[0], b[1], b[2], b[3]);
             }
         }
     };
-    auto take = [&](int i) {
-        const float4* slot = ring + (i & (kRing - 1)) * 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 v = slot[j];
-            r.m[4 * j] = v.x;
-            r.m[4 * j + 1] = v.y;
-            r.m[4 * j + 2] = v.z;
-            r.m[4 * j + 3] = v.w;
-        }
-    };
-    // take(i) as predicated shared loads: r keeps its value where !get.
+    // R and the starting beta of slot i into the lane's registers as
+    // predicated shared loads: they keep their values where !get.
     auto take_if = [&](bool get, int i) {
         const unsigned on = get ? 1u : 0u;
         const unsigned addr =
-            static_cast<unsigned>(__cvta_generic_to_shared(ring + ((i & (kRing - 1)) * 4)));
+            static_cast<unsigned>(__cvta_generic_to_shared(ring + ((i & (kRing - 1)) * kSlot)));
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             asm volatile("{ .reg .pred p; setp.ne.u32 p, %4, 0; @p ld.shared.v4.f32 {%0, %1, %2, %3}, [%5]; }"
                          : "+f"(r.m[4 * j]), "+f"(r.m[4 * j + 1]), "+f"(r.m[4 * j + 2]), "+f"(r.m[4 * j + 3])
                          : "r"(on), "r"(addr + 16u * j)
                          : "memory");
+        asm volatile("{ .reg .pred p; setp.ne.u32 p, %4, 0; @p ld.shared.v4.f32 {%0, %1, %2, %3}, [%5]; }"
+                     : "+f"(beta[0]), "+f"(beta[1]), "+f"(beta[2]), "+f"(beta[3])
+                     : "r"(on), "r"(addr + 64u)
+                     : "memory");
     };
     fill(0);
     fill(kRingHalf);
     __syncwarp();
     int base = 0;  // the ring holds matrices [base, base + kRing)
-    if (idx < cnt) {
-        take(idx);
-        stage = kEval0;
-    } else {
-#pragma unroll
-        for (int e2 = 0; e2 < 16; ++e2) r.m[e2] = 0.0f;
-    }
+    take_if(idx < cnt, idx);
+    if (idx < cnt) stage = kStart;
     int next = min(cnt, 32);
 
     while (__any_sync(kFullMask, stage != kIdle)) {
-        const bool s_eval0 = stage == kEval0, s_alpha0 = stage == kAlpha0, s_evala = stage == kEvalA;
-        const bool s_cand = stage == kCand, s_skcol = stage == kSkCol, s_skeval = stage == kSkEval;
+        const bool s_start = stage == kStart, s_cand = stage == kCand;
+        const bool s_skcol = stage == kSkCol, s_skeval = stage == kSkEval;
 
-        // Direction at the current point; kept only by lanes starting a new
-        // Newton iteration (compute_newton_direction, :443-445).
-        {
-            float dn[4];
-            newton_direction<Rd>(p, c, gn, dn);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) d[j] = sel(fresh, dn[j], d[j]);
-            k = sel(fresh, 0, k);
-            fresh = false;
-        }
-        const bool col = s_alpha0 || s_skcol;
         const float gamma = gtab[k];
-        // Point of evaluation (rows) or per-row offsets (columns).  -0 is the
-        // offset of the alpha = 0 pass: x + (-0) == x for every x, so that pass
-        // sees R itself, as in the reference.
+        // Point of evaluation (rows) or per-row offsets (columns).
         float v[4];
-        const float zero = sel(s_eval0, 0.0f, -0.0f);
-        const bool s_zero = s_eval0 || s_alpha0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const float base = sel(s_skcol, alpha[j], beta[j]);
             const float cand = __fmaf_rn(gamma, d[j], beta[j]);
-            v[j] = sel(s_zero, zero, sel(s_cand, cand, base));
+            v[j] = sel(s_cand, cand, base);
         }
         float X[16];
 #pragma unroll
         for (int l = 0; l < 4; ++l)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) X[4 * l + q] = v[q] + (l == q ? r.m[4 * l + q] : sel(col, r.m[4 * q + l], r.m[4 * l + q]));
+            for (int q = 0; q < 4; ++q)
+                X[4 * l + q] = v[q] + (l == q ? r.m[4 * l + q] : sel(s_skcol, r.m[4 * q + l], r.m[4 * l + q]));
         float e[16], s[4], lse[4];
         lse_pass(X, e, s, lse);
 
@@ -287,51 +268,48 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         const float gnn = __fadd_rn(__fadd_rn(fabsf(cn[0] - 1.0f), fabsf(cn[1] - 1.0f)), fabsf(cn[2] - 1.0f));
         float pn[6];
         gram_sums<Prod>(Tn.m, pn);
-        // Column post-processing: the objective at alpha = 0 (:143); the new
-        // beta = b - b_3 is formed below (:139-146, :168-174).
-        const float fa = -psum4(lse[0], lse[1], lse[2], lse[3]);
 
         // Transition.
         const bool accept = s_cand && fn < f && gnn < gn;
-        const bool adopt = s_eval0 || s_evala || s_skeval || accept;
-        const bool take_a0 = s_alpha0 && fa < f;
-        const bool newbeta = take_a0 || s_skcol;
-#pragma unroll
-        for (int q = 0; q < 6; ++q) p[q] = sel(adopt, pn[q], p[q]);
-#pragma unroll
-        for (int j = 0; j < 3; ++j) c[j] = sel(adopt, cn[j], c[j]);
+        const bool adopt = s_start || s_skeval || accept;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             alpha[j] = sel(adopt, lse[j], alpha[j]);
-            const float bj = lse[j] - lse[3];
-            beta[j] = sel(adopt, v[j], sel(newbeta, bj, beta[j]));
+            // the column half of the sweep gives beta = b - b_3 (:168-174)
+            beta[j] = sel(adopt, v[j], sel(s_skcol, lse[j] - lse[3], beta[j]));
         }
         f = sel(adopt, fn, f);
         gn = sel(adopt, gnn, gn);
         // the first convergence test after initialisation (:426-431), or the
         // test at the end of a Newton iteration (:490-494)
-        const bool check_init = s_evala || (s_alpha0 && !take_a0);
         const bool end_iter = accept || s_skeval;
-        const int it_next = sel(check_init, 0, sel(end_iter, it + 1, it));
-        const bool converged = (check_init || end_iter) && gn < tol;
+        const int it_next = sel(s_start, 0, sel(end_iter, it + 1, it));
+        const bool tested = s_start || end_iter;
+        const bool converged = tested && gn < tol;
         const bool done = converged || (end_iter && it_next == kNewtonMaxIters);
-        const bool next_iter = (check_init || end_iter) && !done;
+        const bool next_iter = tested && !done;
         it = it_next;
         const bool reject_last = s_cand && !accept && k == kLineSearchMaxIters - 1;
-        k = sel(s_cand && !accept, k + 1, k);
-        fresh = next_iter;
+        // Direction at the adopted point, kept by lanes that start a new
+        // Newton iteration (compute_newton_direction, :443-445).
+        {
+            float dn[4];
+            newton_direction<Rd>(pn, cn, gnn, dn);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j] = sel(next_iter, dn[j], d[j]);
+        }
+        k = sel(next_iter, 0, sel(s_cand && !accept, k + 1, k));
         stage = sel(stage == kIdle || done, static_cast<int>(kIdle),
                 sel(next_iter, static_cast<int>(kCand),
-                sel(s_eval0, static_cast<int>(kAlpha0),
-                sel(take_a0, static_cast<int>(kEvalA),
                 sel(reject_last, static_cast<int>(kSkCol),
-                sel(s_skcol, static_cast<int>(kSkEval), stage))))));
+                sel(s_skcol, static_cast<int>(kSkEval), stage))));
 
-        // T leaves with the pass that produced it: predicated stores on the
-        // 16-byte path, so that no branch splits the warp here.
+        // T leaves with the pass that produced it (a row pass: no column pass
+        // ends a matrix): predicated stores on the 16-byte path, so that no
+        // branch splits the warp here.
         Elem* t_at = Tout;
         if constexpr (!kDuals) t_at = reinterpret_cast<Elem*>(warp_pointer());
-        store_elems_if<Elem, kVec>(s_eval0 || (done && !col), t_at, static_cast<int64_t>(idx) * 16, Tn);
+        store_elems_if<Elem, kVec>(done, t_at, static_cast<int64_t>(idx) * 16, Tn);
         if constexpr (kStats) {
             if (done) {
                 iters_out[idx] = it;
@@ -339,8 +317,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             }
         }
         if constexpr (kDuals) {
-            // beta of the output's point: the adopted one (an exit after a
-            // column pass keeps the beta = 0 of the evaluation that wrote T)
+            // beta of the output's point, the adopted one
             store_vec4_if<kVec>(done, reinterpret_cast<float*>(warp_pointer()) + static_cast<int64_t>(idx) * 4,
                                 beta);
         }
@@ -351,7 +328,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         const bool get = done && cand < cnt;
         idx = sel(done, cand, idx);
         take_if(get, cand);
-        stage = sel(get, static_cast<int>(kEval0), stage);
+        stage = sel(get, static_cast<int>(kStart), stage);
         next = min(cnt, next + __popc(want));
         if (next > base + kRingHalf) {  // the older half is all handed out: stage the next one
             __syncwarp();

@@ -206,6 +206,32 @@ __device__ __forceinline__ void lse_pass(const float X[16], float e[16], float s
     }
 }
 
+// The starting point of the Newton solve (birkhoff_proj_n4.cu:400-423): the
+// objective at beta = 0 (rows of 0 + R; the reference's offset is added, so an
+// entry -0 becomes +0 as there) and the alpha = 0 initialisation (column
+// log-sum-exp of R, :129-147), whose beta -- shifted to beta_3 = 0 -- is the
+// start if its objective is strictly lower; beta = 0 otherwise.  The
+// f/gradient evaluation at the start is left to the caller.
+__device__ __forceinline__ void start_point(const float r[16], float beta[4])
+{
+    float X[16], e[16], s[4], lse[4];
+    float z;  // +0, opaque to the compiler so that 0 + R is not folded to R
+    asm("mov.b32 %0, 0;" : "=f"(z));
+#pragma unroll
+    for (int q = 0; q < 16; ++q) X[q] = z + r[q];
+    lse_pass(X, e, s, lse);
+    const float f0 = -psum4(lse[0], lse[1], lse[2], lse[3]) - psum4(z, z, z, z);
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) X[4 * l + q] = r[4 * q + l];
+    lse_pass(X, e, s, lse);
+    const float fa = -psum4(lse[0], lse[1], lse[2], lse[3]);
+    const bool take = fa < f0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) beta[j] = sel(take, lse[j] - lse[3], z);
+}
+
 // Column products of T summed over rows, as the row-0 lanes of the reference
 // hold them (they broadcast H, birkhoff_proj_n4.cu:286-309 and :550-573):
 // p[0..2] = sum_i T_ij^2 for j = 0,1,2 and p[3..5] = sum_i T_ij T_ik for the
