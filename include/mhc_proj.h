@@ -35,7 +35,9 @@ extern "C" {
 enum {
     MHC_OK = 0,
     MHC_ERR_INVALID_VALUE = -1, /* N < 0, a null pointer with N > 0, a negative stride or an unknown dtype */
-    MHC_ERR_ITERS = -2          /* iteration count outside the supported range */
+    MHC_ERR_ITERS = -2,         /* iteration count outside the supported range */
+    MHC_ERR_CAPTURE = -3        /* a first call in a CUDA context that must look up a device
+                                   address was made during stream capture */
 };
 
 /* Storage types of the *_ex entry points.  Computation is always fp32: bf16
@@ -192,9 +194,11 @@ MHC_API int mhc_birkhoff_proj_n4_hres_backward(const float* d_G, const float* d_
  * that is part of the library (1024 rows of 17 floats), which every GPU that
  * loads the library holds until the process exits.  The call uses at most
  * 1024 blocks, one row each, so no batch size needs more than the array.
- * The first call on a device looks the array's address up
- * (cudaGetSymbolAddress) and keeps it; make that first call before any stream
- * capture.  Same results as the workspace form given the size that
+ * The first call in each CUDA context looks the array's address up
+ * (cudaGetSymbolAddress) and keeps it for that context: after a device reset,
+ * or in a context the caller created, the next call looks it up again.  Make
+ * that first call before any stream capture: made during capture it launches
+ * nothing and returns MHC_ERR_CAPTURE.  Same results as the workspace form given the size that
  * mhc_birkhoff_proj_n4_hres_backward_workspace reports (on a GPU whose
  * resident-block wave is at most 1024 blocks, B200 included).  The array is
  * shared by every call on a device and keeps the last call's sums: calls

@@ -1,7 +1,11 @@
 // Kernels and C-ABI launchers for the Newton forward and the IFT backward.
 #include <atomic>
+#include <mutex>
+
+#include <cuda.h>
 
 #include "birkhoff_n4.cuh"
+#include "context_cache.h"
 #include "partial_sums.cuh"
 #include "mhc_proj.h"
 
@@ -565,27 +569,77 @@ static int hres_backward_launch(const float* G, const float* T, const float* h, 
 constexpr int kNoAllocRows = 1024;
 static __device__ __align__(256) float g_hres_partials[kNoAllocRows * kHResPartials];
 
-// Device address of g_hres_partials on the current device.  In host code the
-// array's name is only a host-side stand-in, so the address is looked up
-// (cudaGetSymbolAddress, with the device current) on the first call on each
-// device and kept; the lookup's status is returned as is.
-static cudaError_t noalloc_partials(float** out)
+// The driver's cuCtxGetCurrent and cuCtxGetId, reached through the
+// runtime's driver entry points so that the library needs no link to
+// libcuda.  Resolved once, outside any stream capture.
+struct ContextIdApi {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    GetCurrent get_current = nullptr;
+    GetId get_id = nullptr;
+};
+static std::once_flag g_ctx_api_once;
+static std::atomic<bool> g_ctx_api_ready{false};
+static ContextIdApi g_ctx_api;
+
+static void resolve_context_id_api()
 {
-    static std::atomic<float*> cache[kMaxDevices];
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    float* p = cache[dev].load(std::memory_order_acquire);
-    if (!p) {
-        void* addr = nullptr;
-        e = cudaGetSymbolAddress(&addr, g_hres_partials);
-        if (e != cudaSuccess) return e;
-        p = static_cast<float*>(addr);
-        cache[dev].store(p, std::memory_order_release);
+    std::call_once(g_ctx_api_once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_api.get_current = reinterpret_cast<ContextIdApi::GetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_api.get_id = reinterpret_cast<ContextIdApi::GetId>(f);
+        cudaGetLastError();  // a missing entry point leaves no error behind
+        g_ctx_api_ready.store(true, std::memory_order_release);
+    });
+}
+
+// The process-unique id of the current CUDA context, or 0 when there is none
+// yet or the driver cannot tell.  Needs resolve_context_id_api() first.
+static unsigned long long current_context_id()
+{
+    if (!g_ctx_api.get_current || !g_ctx_api.get_id) return 0;
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_ctx_api.get_current(&ctx) != CUDA_SUCCESS || !ctx || g_ctx_api.get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Device address of g_hres_partials in the current context.  In host code
+// the array's name is only a host-side stand-in, so the address is looked
+// up (cudaGetSymbolAddress, with the device current) on the first call in
+// each context and kept for that context: a device reset or another context
+// on the same device places the array elsewhere and is looked up again.  A
+// call during stream capture uses only a kept address; one that would have
+// to look it up (or, the first time, find the driver's context calls)
+// returns MHC_ERR_CAPTURE instead of doing that inside the capture.
+static int noalloc_partials(cudaStream_t stream, float** out)
+{
+    static ContextCache<kMaxDevices> cache;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    const cudaError_t ce = cudaStreamIsCapturing(stream, &cap);
+    if (ce != cudaSuccess) return static_cast<int>(ce);
+    const bool capturing = cap != cudaStreamCaptureStatusNone;
+    if (!g_ctx_api_ready.load(std::memory_order_acquire)) {
+        if (capturing) return MHC_ERR_CAPTURE;
+        resolve_context_id_api();
     }
-    *out = p;
-    return cudaSuccess;
+    int dev = 0;
+    const cudaError_t de = cudaGetDevice(&dev);
+    if (de != cudaSuccess) return static_cast<int>(de);
+    void* addr = nullptr;
+    const int status = cache.get(dev, current_context_id(), [&](void** v) -> int {
+        if (capturing) return MHC_ERR_CAPTURE;
+        return static_cast<int>(cudaGetSymbolAddress(v, g_hres_partials));
+    }, &addr);
+    if (status != 0) return status;
+    *out = static_cast<float*>(addr);
+    return MHC_OK;
 }
 
 static bool valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
@@ -701,8 +755,8 @@ extern "C" int mhc_birkhoff_proj_n4_hres_backward_noalloc(const float* d_G, cons
         (N > 0 && (!d_G || !d_T || !d_h || !d_rms || !d_alpha || !d_dh || !d_drms)))
         return MHC_ERR_INVALID_VALUE;
     float* partials = nullptr;
-    const cudaError_t se = noalloc_partials(&partials);
-    if (se != cudaSuccess) return static_cast<int>(se);
+    const int se = noalloc_partials(stream, &partials);
+    if (se != MHC_OK) return se;
     // at most kNoAllocRows blocks, each row of the array one block's sums:
     // no batch size needs more scratch than the array holds
     const int blocks = hres_backward_blocks(N, kNoAllocRows);
@@ -745,6 +799,8 @@ extern "C" const char* mhc_status_string(int status)
         case MHC_OK: return "success";
         case MHC_ERR_INVALID_VALUE: return "invalid argument (negative N or stride, null pointer or unknown dtype)";
         case MHC_ERR_ITERS: return "iteration count outside the supported range";
+        case MHC_ERR_CAPTURE:
+            return "first call in this CUDA context made during stream capture; make one call outside capture first";
         default: break;
     }
     if (status > 0) return cudaGetErrorString(static_cast<cudaError_t>(status));

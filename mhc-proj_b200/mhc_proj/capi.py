@@ -40,6 +40,7 @@ _LAUNCHERS = EXPORTED[:-2]
 MHC_OK = 0
 MHC_ERR_INVALID_VALUE = -1
 MHC_ERR_ITERS = -2
+MHC_ERR_CAPTURE = -3
 MHC_SK_BACKWARD_MAX_ITERS = 20
 MHC_DTYPE_F32, MHC_DTYPE_BF16, MHC_DTYPE_F16 = 0, 1, 2
 

@@ -7,8 +7,8 @@ MHCProjectionN4 (lines 73-93) and for the low-level functions (lines
 113-133).  This script reads those printed tensors from the README text and
 writes them to readme_values.json next to it.
 
-Usage (where the reference checkout exists):
-    python tests/golden/make_readme_values.py /root/reference/README.md
+Usage (the path of the reference checkout's README is required):
+    python tests/golden/make_readme_values.py <reference checkout>/README.md
 """
 import json
 import os
@@ -30,7 +30,9 @@ def tensors_after(lines, start, count=32):
 
 
 def main():
-    src = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/README.md"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_readme_values.py <reference checkout>/README.md")
+    src = sys.argv[1]
     lines = open(src).read().splitlines()
     prints = [(i, ln.strip()) for i, ln in enumerate(lines) if ln.startswith("print(")]
     names = ["P_vanilla", "dx_vanilla", "P_module", "dx_module", "P_lowlevel", "D_lowlevel"]
