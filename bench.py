@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
     ap.add_argument("--tol", type=float, default=1e-6)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--mixture-total", type=int, default=1 << 26,
+                    help="matrices of the sharded mixture measurement (total over all ranks; 0 skips it)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -362,20 +364,29 @@ def run_ours(args):
     # end to end through the public API with host buffers: pinned inputs go
     # up, T and D come back, chunks pipelined over two streams
     e2e = run_e2e(args, R, G, dev, world) if args.workload == "newton" else {"ms": float("nan"), "h2d": 0, "d2h": 0, "how": "not measured for this workload"}
+    ceiling_ms = copy_ceiling_ms(args, R, dev, world) if args.workload == "newton" else float("nan")
+    passes = forward_passes(R, tol) if args.workload == "newton" and rank == 0 else None
+    bwd_cold_ms = backward_cold_l2_ms(bwd, fwd, dev) if args.workload == "newton" else float("nan")
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
     if args.workload == "hres":
         unfused_ms, plain_fwd_ms = hres_unfused_ms(hres, G, tol, args.steps)
     if args.workload == "sk_hres":
         unfused_ms = sk_hres_unfused_ms(hres, G, args.steps)
 
-    stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"]], device=dev, dtype=torch.float64)
+    stats = torch.tensor([total_ms, fwd_ms, bwd_ms, e2e["ms"], ceiling_ms, bwd_cold_ms], device=dev,
+                         dtype=torch.float64)
     per_rank = [stats.clone()]
     if world > 1:
         per_rank = [torch.empty_like(stats) for _ in range(world)]
         dist.all_gather(per_rank, stats)
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    total_ms, fwd_ms, bwd_ms, e2e_ms = stats.tolist()
+    total_ms, fwd_ms, bwd_ms, e2e_ms, ceiling_ms, bwd_cold_ms = stats.tolist()
     ms_per_step = total_ms / args.steps
+    del R, G
+    mixture = None
+    if args.workload == "newton" and args.mixture_total > 0:
+        torch.cuda.empty_cache()
+        mixture = sharded_mixture(args, dev, world, rank)
 
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
@@ -423,12 +434,24 @@ def run_ours(args):
                          "algorithmic_bytes_per_matrix": BYTES_FWD + BYTES_BWD},
                 "kernels": {"forward_ms": fwd_ms, "backward_ms": bwd_ms,
                             "forward_gbs": fwd_gbs, "backward_gbs": bwd_gbs,
-                            "backward_frac": bwd_gbs / peak},
+                            "backward_frac": bwd_gbs / peak,
+                            "backward_ms_l2_flushed": bwd_cold_ms,
+                            "backward_frac_l2_flushed": BYTES_BWD * n / (bwd_cold_ms * 1e-3) / 1e9 / peak,
+                            "backward_note": "in the step the backward reads T right after the forward wrote it, "
+                                             "so up to L2's 126 MB of T can be L2 hits; *_l2_flushed times it "
+                                             "after a 512 MiB write evicts L2. Its reads:writes are 2:1, against "
+                                             "the 1:1 of the copy that measured the peak"},
                 "compute": compute,
             },
             "e2e": {"value": world * n / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "ms_per_step": e2e_ms, "how": e2e["how"]},
+                    "ms_per_step": e2e_ms, "how": e2e["how"],
+                    "copy_ceiling": {"value": world * n / (ceiling_ms * 1e-3), "unit": UNIT,
+                                     "ms_per_step": ceiling_ms,
+                                     "host_link_gbs_per_gpu": (e2e["h2d"] + e2e["d2h"]) / (ceiling_ms * 1e-3) / 1e9,
+                                     "how": "the same pinned host<->device copies (same chunks and streams) on every "
+                                            "rank at once with no kernels: what the host links can move"},
+                    "frac_of_copy_ceiling": ceiling_ms / e2e_ms},
             "gpu_launches": 2 * args.steps,
             "clocks": clocks,
             "per_rank": [{"rank": i, "ms_per_step": t[0] / args.steps, "forward_ms": t[1], "backward_ms": t[2]}
@@ -486,6 +509,10 @@ def run_ours(args):
                 "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
                 "how": "H_res = exp(alpha*h/rms + b) with torch ops, sinkhorn_knopp_n4, sinkhorn_knopp_n4_backward, "
                        "then dR = dM*M and dh, drms, dalpha, db with torch ops (this repository's unfused kernels)"}
+        if mixture is not None:
+            line["multi_gpu_mixture"] = mixture
+        if passes is not None:
+            line["forward_passes"] = passes
         rf = line["roofline"]
         rf["nominal"] = {"peak": NOMINAL_HBM_GBS, "unit": "GB/s", "frac": rf["achieved"] / NOMINAL_HBM_GBS,
                          "step_frac": rf["step"]["achieved"] / NOMINAL_HBM_GBS,
@@ -614,6 +641,154 @@ def sinkhorn_unfused_ms(R, G, steps):
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
+
+
+def forward_passes(R, tol):
+    """Where the forward's log-sum-exp passes go on this batch (an untimed run
+    of the counting instantiation), per matrix."""
+    from mhc_proj import capi
+
+    _, _, _, c = capi.birkhoff_proj_n4_pass_counts_tensor(R, tol)
+    m = c["matrices"]
+    per = {k: v / m for k, v in c.items() if k not in ("matrices", "lane_slots", "busy_lane_slots")}
+    state = c["busy_lane_slots"] / m
+    return {"per_matrix": per, "state_machine_passes_per_matrix": state,
+            "passes_per_matrix": state + per["fill"],
+            "lane_utilisation": c["busy_lane_slots"] / c["lane_slots"],
+            "how": "mhc_birkhoff_proj_n4_pass_counts on the timed batch, outside the timed region"}
+
+
+def backward_cold_l2_ms(bwd, fwd, dev, reps: int = 5):
+    """Device time of the backward alone after a 512 MiB write has evicted
+    L2 (so T, written by the forward, comes from HBM)."""
+    import torch
+
+    T = fwd()
+    flush = torch.empty(1 << 27, device=dev)  # 512 MiB, four times L2
+    times = []
+    for _ in range(reps):
+        flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        bwd(T)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1))
+    del flush, T
+    return statistics.median(times)
+
+
+def sharded_mixture(args, dev, world, rank):
+    """The multi-GPU workload as configured: a fixed total of 2^26 matrices of
+    the mixture (50% N(0,1), 25% N(0,9), 25% N(0,1) with +6 on one entry per
+    row), G ~ N(0,1), split into contiguous shards over the ranks
+    (mhc_proj.sharding.shard_range); each rank runs fwd+bwd on its shard.
+    Every rank generates the whole batch from the same seeds and keeps its
+    slice, so a matrix has the same logits at every world size.  Device time
+    over the timed steps, barrier and synchronize around them, max over ranks;
+    value = total / slowest rank's step."""
+    import torch
+    import torch.distributed as dist
+
+    import mhc_proj
+    from mhc_proj.sharding import shard_range
+    from mhc_proj.workloads import make_logits
+
+    total = args.mixture_total
+    a, b = shard_range(total, rank, world)
+    R = make_logits("mixture", total, seed=500, device=dev)[a:b].clone()
+    torch.cuda.empty_cache()
+    G = make_logits("normal", total, seed=501, device=dev)[a:b].clone()
+    torch.cuda.empty_cache()
+    steps = 3
+
+    def step(ev):
+        ev[0].record()
+        T = mhc_proj.torch.birkhoff_proj_n4(R, args.tol)["T"]
+        ev[1].record()
+        mhc_proj.torch.birkhoff_proj_n4_backward(G, T)["D"]
+        ev[2].record()
+
+    warm = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    step(warm)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(evs[i])
+    t1.record()
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / steps
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / steps
+    mine = torch.tensor([ms, fwd_ms, bwd_ms, float(b - a)], device=dev, dtype=torch.float64)
+    ranks = [mine]
+    if world > 1:
+        ranks = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(ranks, mine)
+    ranks = [r.tolist() for r in ranks]
+    del R, G
+    torch.cuda.empty_cache()
+    slow = max(range(world), key=lambda i: ranks[i][0])
+    per_gpu = [{"rank": i, "matrices": int(r[3]), "ms_per_step": r[0], "forward_ms": r[1], "backward_ms": r[2],
+                "hbm_gbs": (BYTES_FWD + BYTES_BWD) * r[3] / (r[0] * 1e-3) / 1e9}
+               for i, r in enumerate(ranks)]
+    return {"workload": f"Newton forward (tol {args.tol:g}) + IFT backward on N=2^{total.bit_length() - 1} "
+                        f"matrices in total of the mixture (50% N(0,1), 25% N(0,9), 25% N(0,1)+6 on one entry "
+                        f"per row), G~N(0,1), batch-sharded over {world} GPU(s)",
+            "total_matrices": total, "value": total / (ranks[slow][0] * 1e-3), "unit": UNIT,
+            "scaling": "strong", "slowest_rank": slow, "ms_per_step": ranks[slow][0], "steps": steps,
+            "per_gpu": per_gpu}
+
+
+def copy_ceiling_ms(args, R, dev, world):
+    """Per-step device time of run_e2e's host<->device copies alone (same
+    chunks, streams and pinned buffers, no kernels), on every rank at once."""
+    import torch
+
+    n = R.shape[0]
+    chunks = 16 if n >= (1 << 20) else 1
+    Rh = torch.empty((n, 4, 4), dtype=R.dtype).pin_memory()
+    Gh = torch.empty_like(Rh).pin_memory()
+    Th = torch.empty_like(Rh).pin_memory()
+    Dh = torch.empty_like(Rh).pin_memory()
+    Rd = torch.empty_like(R)
+    Gd = torch.empty_like(R)
+    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
+    bounds = [(n * i // chunks, n * (i + 1) // chunks) for i in range(chunks)]
+
+    def step():
+        for i, (a, b) in enumerate(bounds):
+            s = streams[i % len(streams)]
+            with torch.cuda.stream(s):
+                Rd[a:b].copy_(Rh[a:b], non_blocking=True)
+                Gd[a:b].copy_(Gh[a:b], non_blocking=True)
+                Th[a:b].copy_(Rd[a:b], non_blocking=True)
+                Dh[a:b].copy_(Gd[a:b], non_blocking=True)
+        for s in streams:
+            torch.cuda.current_stream(dev).wait_stream(s)
+
+    step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[dev.index])
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.e2e_steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / args.e2e_steps
 
 
 def run_e2e(args, R, G, dev, world):

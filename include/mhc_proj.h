@@ -71,6 +71,35 @@ MHC_API int mhc_birkhoff_proj_n4(const float* d_R, float* d_T, float tol, int64_
 MHC_API int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float tol, int64_t N,
                                        int32_t* d_iters, float* d_gnorm, cudaStream_t stream);
 
+/* Counters of mhc_birkhoff_proj_n4_pass_counts: where the forward's
+ * log-sum-exp passes go.  Each matrix costs two passes when it is staged
+ * (the beta = 0 objective and the alpha = 0 initialisation,
+ * src/birkhoff_proj_n4.cu:402-415), then one pass per step of its state
+ * machine: the evaluation at the chosen start (:416-423), line-search
+ * candidates k = 0..4 (:450-477), and the two passes of a Sinkhorn sweep
+ * after five rejections (:480-486). */
+enum {
+    MHC_PASS_MATRICES = 0,        /* matrices projected */
+    MHC_PASS_FILL = 1,            /* passes made while staging (2 per matrix) */
+    MHC_PASS_START = 2,           /* evaluations at the starting point */
+    MHC_PASS_CANDIDATE = 3,       /* + k, k = 0..4: candidate evaluations at step gamma_k */
+    MHC_PASS_ACCEPTED = 8,        /* + k: candidates accepted at step gamma_k */
+    MHC_PASS_SWEEP_COLUMN = 13,   /* column passes of the Sinkhorn fallback sweep */
+    MHC_PASS_SWEEP_EVAL = 14,     /* evaluations after the sweep */
+    MHC_PASS_AT_CAP = 15,         /* matrices that stopped at the 20-iteration cap */
+    MHC_PASS_LANE_SLOTS = 16,     /* state-machine steps x 32 lanes */
+    MHC_PASS_BUSY_LANE_SLOTS = 17, /* lane slots that held a matrix (the rest: a warp's tail) */
+    MHC_PASS_COUNTERS = 18
+};
+
+/* mhc_birkhoff_proj_n4_stats that also adds the forward's pass counts to
+ * d_counts[MHC_PASS_COUNTERS] (64-bit, accumulated: zero it first).  A
+ * diagnostic of the state machine's work, in an instantiation of its own;
+ * T is the same as from mhc_birkhoff_proj_n4.  No reference counterpart. */
+MHC_API int mhc_birkhoff_proj_n4_pass_counts(const float* d_R, float* d_T, float tol, int64_t N,
+                                             int32_t* d_iters, float* d_gnorm, unsigned long long* d_counts,
+                                             cudaStream_t stream);
+
 /* mhc_birkhoff_proj_n4 that also writes, per matrix, the final dual beta
  * (4 floats at d_beta + 4k, beta[3] = 0 up to its sign): T is exactly
  * row-softmax(beta + R), which mhc_birkhoff_proj_n4_backward_duals rebuilds

@@ -127,7 +127,8 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
 // kStats: also write, per matrix, the number of Newton iterations taken and
-// the final gradient l1 norm; kDuals: also write the final beta (4 floats,
+// the final gradient l1 norm, and, when `counts` is given, add the warp's
+// pass counts by stage to it (MHC_PASS_* in mhc_proj.h); kDuals: also write the final beta (4 floats,
 // the point whose T is the output: T = row-softmax(beta + R)).  Separate
 // instantiations; the plain one carries no cost for either.
 template <class Rd, class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
@@ -135,7 +136,8 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
                                                                     int64_t N, int64_t per_warp,
                                                                     int32_t* __restrict__ iters_out = nullptr,
                                                                     float* __restrict__ gnorm_out = nullptr,
-                                                                    float* __restrict__ beta_out = nullptr)
+                                                                    float* __restrict__ beta_out = nullptr,
+                                                                    unsigned long long* __restrict__ counts = nullptr)
 {
     using Prod = typename Rd::P;
     const int lane = threadIdx.x & 31;
@@ -233,6 +235,8 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     take_if(idx < cnt, idx);
     if (idx < cnt) stage = kStart;
     int next = min(cnt, 32);
+    // kStats with counts: the warp's pass counts, the same in every lane
+    unsigned tally[MHC_PASS_COUNTERS] = {};
 
     while (__any_sync(kFullMask, stage != kIdle)) {
         const bool s_start = stage == kStart, s_cand = stage == kCand;
@@ -294,6 +298,23 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         const bool next_iter = tested && !done;
         it = it_next;
         const bool reject_last = s_cand && !accept && k == kLineSearchMaxIters - 1;
+        if constexpr (kStats) {
+            if (counts) {
+                auto add = [&](int q, bool b) { tally[q] += __popc(__ballot_sync(kFullMask, b)); };
+                const bool busy = stage != kIdle;
+                tally[MHC_PASS_LANE_SLOTS] += 32;
+                add(MHC_PASS_BUSY_LANE_SLOTS, busy);
+                add(MHC_PASS_START, s_start);
+#pragma unroll
+                for (int q = 0; q < kLineSearchMaxIters; ++q) {
+                    add(MHC_PASS_CANDIDATE + q, s_cand && k == q);
+                    add(MHC_PASS_ACCEPTED + q, accept && k == q);
+                }
+                add(MHC_PASS_SWEEP_COLUMN, s_skcol);
+                add(MHC_PASS_SWEEP_EVAL, s_skeval);
+                add(MHC_PASS_AT_CAP, busy && done && !converged);
+            }
+        }
         // Direction at the adopted point, kept by lanes that start a new
         // Newton iteration (compute_newton_direction, :443-445).
         {
@@ -339,6 +360,14 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
             fill(base + kRing);
             __syncwarp();
             base += kRingHalf;
+        }
+    }
+    if constexpr (kStats) {
+        if (counts && lane == 0) {
+            tally[MHC_PASS_MATRICES] = static_cast<unsigned>(cnt);
+            tally[MHC_PASS_FILL] = 2u * static_cast<unsigned>(cnt);
+            for (int q = 0; q < MHC_PASS_COUNTERS; ++q)
+                if (tally[q]) atomicAdd(counts + q, static_cast<unsigned long long>(tally[q]));
         }
     }
 }
@@ -464,7 +493,7 @@ static int64_t forward_warp_slots()
 
 template <class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
 static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters = nullptr,
-                          float* gnorm = nullptr, float* beta = nullptr)
+                          float* gnorm = nullptr, float* beta = nullptr, unsigned long long* counts = nullptr)
 {
     constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats, kDuals>;
     const int64_t slots = forward_warp_slots<kernel>();
@@ -478,7 +507,8 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     const int64_t per_warp = ceil_div(N, warps);
     const int64_t used = ceil_div(N, per_warp);
     const int64_t grid = ceil_div(used * 32, kNewtonBlock);
-    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm, beta);
+    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm, beta,
+                                              counts);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -675,6 +705,19 @@ extern "C" int mhc_birkhoff_proj_n4_stats(const float* d_R, float* d_T, float to
                                                                              d_gnorm)
                : launch_forward<DenseSource<float, false>, float, false, true>({d_R, 16}, d_T, tol, N, stream,
                                                                                d_iters, d_gnorm);
+}
+
+extern "C" int mhc_birkhoff_proj_n4_pass_counts(const float* d_R, float* d_T, float tol, int64_t N,
+                                                int32_t* d_iters, float* d_gnorm, unsigned long long* d_counts,
+                                                cudaStream_t stream)
+{
+    if (N < 0 || (N > 0 && (!d_R || !d_T || !d_iters || !d_gnorm || !d_counts))) return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    return aligned16(d_R) && aligned16(d_T)
+               ? launch_forward<DenseSource<float, true>, float, true, true>({d_R, 16}, d_T, tol, N, stream, d_iters,
+                                                                             d_gnorm, nullptr, d_counts)
+               : launch_forward<DenseSource<float, false>, float, false, true>({d_R, 16}, d_T, tol, N, stream,
+                                                                               d_iters, d_gnorm, nullptr, d_counts);
 }
 
 extern "C" int mhc_birkhoff_proj_n4_backward_ex(const void* d_G, int64_t g_stride, int g_dtype, const void* d_T,

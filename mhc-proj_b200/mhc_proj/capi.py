@@ -19,6 +19,7 @@ EXPORTED = (
     "mhc_birkhoff_proj_n4_ex",
     "mhc_birkhoff_proj_n4_backward_ex",
     "mhc_birkhoff_proj_n4_stats",
+    "mhc_birkhoff_proj_n4_pass_counts",
     "mhc_birkhoff_proj_n4_duals",
     "mhc_birkhoff_proj_n4_backward_duals",
     "mhc_sinkhorn_knopp_n4",
@@ -68,6 +69,7 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_ex.argtypes = [vp, i64, vp, i32, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_backward_ex.argtypes = [vp, i64, i32, vp, i64, i32, vp, i64, vp]
         L.mhc_birkhoff_proj_n4_stats.argtypes = [vp, vp, f32, i64, vp, vp, vp]
+        L.mhc_birkhoff_proj_n4_pass_counts.argtypes = [vp, vp, f32, i64, vp, vp, vp, vp]
         L.mhc_birkhoff_proj_n4_duals.argtypes = [vp, vp, vp, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_backward_duals.argtypes = [vp, vp, vp, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
@@ -115,6 +117,12 @@ def birkhoff_proj_n4_backward(G: int, T: int, D: int, N: int, stream: int = 0) -
 
 def birkhoff_proj_n4_stats(R: int, T: int, tol: float, N: int, iters: int, gnorm: int, stream: int = 0) -> None:
     _check(lib().mhc_birkhoff_proj_n4_stats(R, T, tol, N, iters, gnorm, stream), "mhc_birkhoff_proj_n4_stats")
+
+
+def birkhoff_proj_n4_pass_counts(R: int, T: int, tol: float, N: int, iters: int, gnorm: int, counts: int,
+                                 stream: int = 0) -> None:
+    _check(lib().mhc_birkhoff_proj_n4_pass_counts(R, T, tol, N, iters, gnorm, counts, stream),
+           "mhc_birkhoff_proj_n4_pass_counts")
 
 
 def birkhoff_proj_n4_duals(R: int, T: int, beta: int, tol: float, N: int, stream: int = 0) -> None:
@@ -236,6 +244,29 @@ def birkhoff_proj_n4_backward_tensor(G, T, out=None):
     D = torch.empty_like(G) if out is None else out
     birkhoff_proj_n4_backward(_dev(G, "G"), _dev(T, "T"), _dev(D, "D"), G.shape[0], _stream(G))
     return D
+
+
+# Order of the counters of mhc_birkhoff_proj_n4_pass_counts (MHC_PASS_* in mhc_proj.h).
+PASS_COUNTER_NAMES = ("matrices", "fill", "start", "candidate_0", "candidate_1", "candidate_2", "candidate_3",
+                      "candidate_4", "accepted_0", "accepted_1", "accepted_2", "accepted_3", "accepted_4",
+                      "sweep_column", "sweep_eval", "at_cap", "lane_slots", "busy_lane_slots")
+
+
+def birkhoff_proj_n4_pass_counts_tensor(R, tol: float = 1e-6):
+    """Forward of a contiguous fp32 CUDA batch R through the counting
+    instantiation: returns (T, iters, gnorm, counts) with counts a dict of
+    the MHC_PASS_* totals (Python ints)."""
+    import torch
+
+    _dev(R, "R")
+    n = R.shape[0]
+    T = torch.empty_like(R)
+    it = torch.empty(n, dtype=torch.int32, device=R.device)
+    gn = torch.empty(n, dtype=torch.float32, device=R.device)
+    c = torch.zeros(len(PASS_COUNTER_NAMES), dtype=torch.int64, device=R.device)
+    birkhoff_proj_n4_pass_counts(R.data_ptr(), T.data_ptr(), tol, n, it.data_ptr(), gn.data_ptr(), c.data_ptr(),
+                                 _stream(R))
+    return T, it, gn, dict(zip(PASS_COUNTER_NAMES, (int(v) for v in c.tolist())))
 
 
 def birkhoff_proj_n4_duals_tensor(R, tol: float = 1e-6):
