@@ -37,6 +37,9 @@ def _load():
         lib.oracle_max_threads.restype = ctypes.c_int
         lib.oracle_birkhoff_proj_n4.argtypes = [_f32p, _f32p, ctypes.c_float, ctypes.c_int64, _i32p, ctypes.c_int]
         lib.oracle_birkhoff_proj_n4.restype = None
+        lib.oracle_birkhoff_proj_n4_line_search.argtypes = [_f32p, _f32p, ctypes.c_float, ctypes.c_int64,
+                                                            ctypes.c_int, _i32p, ctypes.c_int]
+        lib.oracle_birkhoff_proj_n4_line_search.restype = ctypes.c_int
         lib.oracle_birkhoff_proj_n4_backward.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int]
         lib.oracle_birkhoff_proj_n4_backward.restype = None
         lib.oracle_sinkhorn_knopp_n4.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int]
@@ -73,6 +76,21 @@ def birkhoff_proj_n4(R, tol=1e-6, threads=0, return_evals=False):
     _load().oracle_birkhoff_proj_n4(_p(R), _p(T), float(tol), N,
                                     ev.ctypes.data_as(_i32p) if ev is not None else None, int(threads))
     return (T, ev) if return_evals else T
+
+
+def birkhoff_proj_n4_line_search(R, candidates, tol=1e-6, threads=0):
+    """The Newton forward with its line search cut to the first `candidates`
+    steps of (1, 0.5, 0.1, 0.05, 0.01) before the Sinkhorn fallback (5 = the
+    reference, birkhoff_proj_n4.cu:434-487).  Returns (T, Newton iterations
+    per matrix).  A study tool: fewer candidates is a different trajectory."""
+    R = _as_batch(R, "R")
+    N = R.shape[0]
+    T = np.empty_like(R)
+    it = np.empty(N, dtype=np.int32)
+    if _load().oracle_birkhoff_proj_n4_line_search(_p(R), _p(T), float(tol), N, int(candidates),
+                                                    it.ctypes.data_as(_i32p), int(threads)) != 0:
+        raise ValueError("candidates must be 1..5")
+    return T, it
 
 
 def birkhoff_proj_n4_backward(G, T, threads=0):

@@ -200,9 +200,12 @@ static void newton_direction(const fg_state* s, float d[4])
     for (int j = 0; j < 3; j++) d[j] = -y[j] / det;
 }
 
-/* birkhoff_proj_n4_kernel, birkhoff_proj_n4.cu:375-499, for one matrix.
- * Returns the number of f/gradient evaluations spent (a cost measure). */
-static int newton_one(const float R[16], float T[16], float tol)
+/* birkhoff_proj_n4_kernel, birkhoff_proj_n4.cu:375-499, for one matrix, with
+ * the line search cut to its first `candidates` steps (5 = the reference;
+ * fewer gives the shortened trajectories a study compares with it).  Returns
+ * the number of f/gradient evaluations spent (a cost measure); *iters_out,
+ * when given, receives the Newton iterations taken. */
+static int newton_one_ls(const float R[16], float T[16], float tol, int candidates, int* iters_out)
 {
     static const float gamma_list[LINE_SEARCH_MAX_ITERS] = {1.0f, 0.5f, 0.1f, 0.05f, 0.01f};
     float beta[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -218,11 +221,13 @@ static int newton_one(const float R[16], float T[16], float tol)
         eval_f_grad(beta, R, &cur);
         evals++;
     }
+    int iters = 0;
     if (!(cur.gnorm < tol)) {
         for (int it = 0; it < NEWTON_MAX_ITERS; it++) {
             float d[4];
+            iters = it + 1;
             newton_direction(&cur, d);
-            for (int k = 0; k < LINE_SEARCH_MAX_ITERS; k++) {
+            for (int k = 0; k < candidates; k++) {
                 const float gamma = gamma_list[k];
                 float bc[4];
                 for (int j = 0; j < 4; j++) bc[j] = fmaf(gamma, d[j], beta[j]);
@@ -233,7 +238,7 @@ static int newton_one(const float R[16], float T[16], float tol)
                     cur = cand;
                     break;
                 }
-                if (k == LINE_SEARCH_MAX_ITERS - 1) {
+                if (k == candidates - 1) {
                     sinkhorn_sweep(beta, R);
                     eval_f_grad(beta, R, &cur);
                     evals += 2;
@@ -243,7 +248,13 @@ static int newton_one(const float R[16], float T[16], float tol)
         }
     }
     memcpy(T, cur.T, sizeof(cur.T));
+    if (iters_out) *iters_out = iters;
     return evals;
+}
+
+static int newton_one(const float R[16], float T[16], float tol)
+{
+    return newton_one_ls(R, T, tol, LINE_SEARCH_MAX_ITERS, NULL);
 }
 
 /* birkhoff_proj_n4_backward_kernel, birkhoff_proj_n4.cu:619-669 with
@@ -435,6 +446,28 @@ void oracle_birkhoff_proj_n4(const float* R, float* T, float tol, int64_t N,
 {
     newton_ctx c = {R, T, tol, evals};
     run_batch(newton_range, &c, N, nthreads);
+}
+
+typedef struct { const float* R; float* T; float tol; int candidates; int32_t* iters; } newton_ls_ctx;
+static void newton_ls_range(void* p, int64_t b0, int64_t b1)
+{
+    newton_ls_ctx* c = (newton_ls_ctx*)p;
+    for (int64_t b = b0; b < b1; b++) {
+        int it = 0;
+        newton_one_ls(c->R + 16 * b, c->T + 16 * b, c->tol, c->candidates, &it);
+        if (c->iters) c->iters[b] = it;
+    }
+}
+
+/* The forward with the line search cut to `candidates` steps (1..5; 5 is
+ * the reference).  Returns -1 for a count outside 1..5. */
+int oracle_birkhoff_proj_n4_line_search(const float* R, float* T, float tol, int64_t N, int candidates,
+                                        int32_t* iters, int nthreads)
+{
+    if (candidates < 1 || candidates > LINE_SEARCH_MAX_ITERS) return -1;
+    newton_ls_ctx c = {R, T, tol, candidates, iters};
+    run_batch(newton_ls_range, &c, N, nthreads);
+    return 0;
 }
 
 typedef struct { const float* G; const float* T; float* D; } ift_ctx;
