@@ -372,6 +372,144 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     }
 }
 
+// Small batches: two lanes per matrix.  A batch that fills only a fraction
+// of one wave leaves each warp alone on its SM sub-partition, and the kernel
+// lasts as long as its slowest matrix's passes times the latency of one step
+// of a lone warp.  Here the two lanes of a pair each take two of the four
+// lines of every pass -- rows 2h, 2h+1 of a row pass, columns 2h, 2h+1 of a
+// column pass -- and exchange their half of each sum over the matrix with
+// one shuffle: the reference's order (r0 + r1) + (r2 + r3) is kept, because
+// lane 0 holds the first pair's sum and lane 1 the second's, and an IEEE sum
+// of the two is the same in either order.  Both lanes then hold the same
+// column sums, Gram sums, f and |g|, and compute the same direction.  The
+// state machine is the persistent kernel's without the ring: each pair owns
+// one matrix, which it stores (its two rows each) when it finishes.
+template <class Rd, class Src, class Elem, bool kVec>
+__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_pair_kernel(Src src, Elem* __restrict__ Tout, float tol,
+                                                                         int64_t N)
+{
+    const int64_t m = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 1;
+    const bool h = (threadIdx.x & 1) != 0;  // second lane of the pair: lines 2, 3
+    const bool live = m < N;
+    float rows[8], cols[8];  // this lane's two rows and two columns of R
+    {
+        Mat4 r = {};
+        if (live) {
+            src.advance(m);
+            src.load(0, r);
+        }
+#pragma unroll
+        for (int l = 0; l < 2; ++l)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                rows[4 * l + q] = sel(h, r.m[4 * (2 + l) + q], r.m[4 * l + q]);
+                cols[4 * l + q] = sel(h, r.m[4 * q + 2 + l], r.m[4 * q + l]);
+            }
+    }
+    auto other = [](float x) { return __shfl_xor_sync(kFullMask, x, 1); };
+    // The four lines' values from this lane's two: lines 0, 1 from lane 0.
+    auto all4 = [&](const float (&mine)[2], float (&a)[4]) {
+#pragma unroll
+        for (int l = 0; l < 2; ++l) {
+            const float t = other(mine[l]);
+            a[l] = sel(h, t, mine[l]);
+            a[2 + l] = sel(h, mine[l], t);
+        }
+    };
+    auto half_sum = [&](float mine) { return __fadd_rn(mine, other(mine)); };
+
+    float X[8], e[8], s[2], ls[2], lse[4];
+    float beta[4];
+    {
+        // the starting point (birkhoff_proj_n4.cu:400-423), as start_point
+        float z;
+        asm("mov.b32 %0, 0;" : "=f"(z));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) X[q] = z + rows[q];
+        lse_lines<2>(X, e, s, ls);
+        all4(ls, lse);
+        const float f0 = -psum4(lse[0], lse[1], lse[2], lse[3]) - psum4(z, z, z, z);
+        lse_lines<2>(cols, e, s, ls);
+        all4(ls, lse);
+        const float fa = -psum4(lse[0], lse[1], lse[2], lse[3]);
+        const bool take = fa < f0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) beta[j] = sel(take, lse[j] - lse[3], z);
+    }
+
+    float f = 0.0f, gn = 0.0f;
+    float alpha[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int k = 0, it = 0;
+    int stage = live ? kStart : kIdle;
+    while (__any_sync(kFullMask, stage != kIdle)) {
+        const bool s_start = stage == kStart, s_cand = stage == kCand;
+        const bool s_skcol = stage == kSkCol, s_skeval = stage == kSkEval;
+        const float gamma = line_step(k);
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            v[j] = sel(s_cand, __fmaf_rn(gamma, d[j], beta[j]), sel(s_skcol, alpha[j], beta[j]));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) X[q] = v[q & 3] + sel(s_skcol, cols[q], rows[q]);
+        lse_lines<2>(X, e, s, ls);
+        all4(ls, lse);
+
+        // this lane's two rows of T, then the sums over all four rows
+        float t[8];
+#pragma unroll
+        for (int l = 0; l < 2; ++l) {
+            const float rs = fast_rcp(s[l]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) t[4 * l + q] = __fmul_rn(e[4 * l + q], rs);
+        }
+        float cn[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) cn[j] = half_sum(__fadd_rn(t[j], t[4 + j]));
+        const float fn = -psum4(lse[0], lse[1], lse[2], lse[3]) - psum4(v[0], v[1], v[2], v[3]);
+        const float gnn = __fadd_rn(__fadd_rn(fabsf(cn[0] - 1.0f), fabsf(cn[1] - 1.0f)), fabsf(cn[2] - 1.0f));
+        float pn[6];
+        {
+            constexpr int J[6] = {0, 1, 2, 0, 1, 2};
+            constexpr int K[6] = {0, 1, 2, 1, 2, 0};
+#pragma unroll
+            for (int q = 0; q < 6; ++q)
+                pn[q] = half_sum(__fadd_rn(__fmul_rn(t[J[q]], t[K[q]]), __fmul_rn(t[4 + J[q]], t[4 + K[q]])));
+        }
+
+        // Transition, as in birkhoff_fwd_kernel.
+        const bool accept = s_cand && fn < f && gnn < gn;
+        const bool adopt = s_start || s_skeval || accept;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            alpha[j] = sel(adopt, lse[j], alpha[j]);
+            beta[j] = sel(adopt, v[j], sel(s_skcol, lse[j] - lse[3], beta[j]));
+        }
+        f = sel(adopt, fn, f);
+        gn = sel(adopt, gnn, gn);
+        const bool end_iter = accept || s_skeval;
+        const int it_next = sel(s_start, 0, sel(end_iter, it + 1, it));
+        const bool tested = s_start || end_iter;
+        const bool converged = tested && gn < tol;
+        const bool done = converged || (end_iter && it_next == kNewtonMaxIters);
+        const bool next_iter = tested && !done;
+        it = it_next;
+        const bool reject_last = s_cand && !accept && k == kLineSearchMaxIters - 1;
+        {
+            float dn[4];
+            newton_direction<Rd>(pn, cn, gnn, dn);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j] = sel(next_iter, dn[j], d[j]);
+        }
+        k = sel(next_iter, 0, sel(s_cand && !accept, k + 1, k));
+        stage = sel(stage == kIdle || done, static_cast<int>(kIdle),
+                sel(next_iter, static_cast<int>(kCand),
+                sel(reject_last, static_cast<int>(kSkCol),
+                sel(s_skcol, static_cast<int>(kSkEval), stage))));
+        if (done) store_rows2<Elem, kVec>(Tout + m * 16 + (h ? 8 : 0), t);
+    }
+}
+
 // T = row-softmax(beta + R) with the forward's arithmetic, so that a T
 // rebuilt from the saved beta is the forward's output bit for bit.
 __device__ __forceinline__ void rebuild_t(const Mat4& r, const float (&beta)[4], Mat4& T)
@@ -512,11 +650,29 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     return static_cast<int>(cudaGetLastError());
 }
 
+// Batches up to this many matrices take the two-lanes-per-matrix kernel.
+#ifndef MHC_PAIR_MAX_N
+#define MHC_PAIR_MAX_N (int64_t{1} << 13)
+#endif
+constexpr int64_t kPairMaxN = MHC_PAIR_MAX_N;
+
+template <class Src, class Elem, bool kVec>
+static int launch_forward_pairs(Src src, void* T, float tol, int64_t N, cudaStream_t stream)
+{
+    const int64_t grid = ceil_div(2 * N, kNewtonBlock);
+    birkhoff_fwd_pair_kernel<RefRounding, Src, Elem, kVec>
+        <<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N);
+    return static_cast<int>(cudaGetLastError());
+}
+
 template <class Elem>
 static int forward_typed(const void* R, int64_t r_stride, void* T, float tol, int64_t N, cudaStream_t stream)
 {
     const Elem* r = static_cast<const Elem*>(R);
     const bool vec = aligned16(R, r_stride, sizeof(Elem)) && aligned16(T);
+    if (N <= kPairMaxN)
+        return vec ? launch_forward_pairs<DenseSource<Elem, true>, Elem, true>({r, r_stride}, T, tol, N, stream)
+                   : launch_forward_pairs<DenseSource<Elem, false>, Elem, false>({r, r_stride}, T, tol, N, stream);
     return vec ? launch_forward<DenseSource<Elem, true>, Elem, true>({r, r_stride}, T, tol, N, stream)
                : launch_forward<DenseSource<Elem, false>, Elem, false>({r, r_stride}, T, tol, N, stream);
 }

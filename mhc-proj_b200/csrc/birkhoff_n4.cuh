@@ -206,6 +206,21 @@ __device__ __forceinline__ void lse_pass(const float X[16], float e[16], float s
     }
 }
 
+// lse_pass on L lines (the small-batch kernel's lanes take two each).
+template <int L>
+__device__ __forceinline__ void lse_lines(const float* X, float* e, float* s, float* lse)
+{
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+        const float* x = X + 4 * l;
+        const float mx = pmax4(x[0], x[1], x[2], x[3]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) e[4 * l + k] = expf(x[k] - mx);
+        s[l] = psum4(e[4 * l], e[4 * l + 1], e[4 * l + 2], e[4 * l + 3]);
+        lse[l] = -mx - logf(s[l]);
+    }
+}
+
 // The starting point of the Newton solve (birkhoff_proj_n4.cu:400-423): the
 // objective at beta = 0 (rows of 0 + R; the reference's offset is added, so an
 // entry -0 becomes +0 as there) and the alpha = 0 initialisation (column

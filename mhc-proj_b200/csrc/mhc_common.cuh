@@ -189,6 +189,27 @@ __device__ __forceinline__ void store_elems_if(bool pred, Elem* __restrict__ bas
     }
 }
 
+// Two consecutive rows (8 entries) of a matrix at p, stored as Elem: two
+// 16-byte stores (fp32) or one (bf16/fp16) on the aligned path.
+template <class Elem, bool kVec>
+__device__ __forceinline__ void store_rows2(Elem* __restrict__ p, const float (&t)[8])
+{
+    if constexpr (kVec && sizeof(Elem) == 4) {
+        float4* q = reinterpret_cast<float4*>(p);
+        __stcs(q, make_float4(t[0], t[1], t[2], t[3]));
+        __stcs(q + 1, make_float4(t[4], t[5], t[6], t[7]));
+    } else if constexpr (kVec) {
+        uint4 v;
+        Elem* e = reinterpret_cast<Elem*>(&v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = from_f32<Elem>(t[k]);
+        __stcs(reinterpret_cast<uint4*>(p), v);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) p[k] = from_f32<Elem>(t[k]);
+    }
+}
+
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
