@@ -368,6 +368,7 @@ def run_ours(args):
     passes = forward_passes(R, tol) if args.workload == "newton" and rank == 0 else None
     bwd_cold_ms = backward_cold_l2_ms(bwd, fwd, dev) if args.workload == "newton" else float("nan")
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
+    hw_rcp_fwd_ms = sinkhorn_hw_reciprocal_fwd_ms(R, args.steps) if args.workload == "sinkhorn" else None
     if args.workload == "hres":
         unfused_ms, plain_fwd_ms = hres_unfused_ms(hres, G, tol, args.steps)
     if args.workload == "sk_hres":
@@ -462,6 +463,11 @@ def run_ours(args):
             line["roofline"]["compute"] = None
             line["roofline"]["traffic"] = None
             line["e2e"] = None
+            line["forward_hw_reciprocal"] = {
+                "forward_ms": hw_rcp_fwd_ms, "step_ms": hw_rcp_fwd_ms + bwd_ms,
+                "value": n / ((hw_rcp_fwd_ms + bwd_ms) * 1e-3),
+                "how": "the opt-in forward with the hardware reciprocal (MHC_SK_HW_RECIPROCAL; within 1e-6 of "
+                       "the default forward's bits) with the same backward"}
             line["unfused_reference_composition"] = {
                 "ms_per_step": unfused_ms, "value": n / (unfused_ms * 1e-3),
                 "how": "torch.exp, sinkhorn_knopp_n4, sinkhorn_knopp_n4_backward, product with exp(R) "
@@ -604,6 +610,29 @@ def sk_hres_unfused_ms(hres, G, steps):
         s = a / rms
         q = (dR * h).sum(1)
         return dR * s[:, None], -(s / rms) * q, (q / rms).sum(), dR.sum(0)
+
+    for _ in range(3):
+        once()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        once()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def sinkhorn_hw_reciprocal_fwd_ms(R, steps):
+    """Device time of the fused Sinkhorn-Knopp forward with the hardware
+    reciprocal (the opt-in MHC_SK_HW_RECIPROCAL)."""
+    import torch
+
+    import mhc_proj
+
+    def once():
+        return mhc_proj.torch.sinkhorn_knopp_n4_logits(R, 20, approx_reciprocal=True)["T"]
 
     for _ in range(3):
         once()

@@ -167,6 +167,20 @@ MHC_API int mhc_sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M, f
 MHC_API int mhc_sinkhorn_knopp_n4_logits(const float* d_R, float* d_T, int64_t N, int num_iters,
                                          cudaStream_t stream);
 
+/* Flags of mhc_sinkhorn_knopp_n4_logits_ex. */
+enum {
+    /* The normalisation factors from the hardware reciprocal (at most one
+     * ulp from 1/s) instead of the correctly rounded one: not the reference
+     * kernel's bits, but within 1e-6 of them and of the vanilla PyTorch
+     * Sinkhorn-Knopp on N(0,1) logits, and about 20% faster. */
+    MHC_SK_HW_RECIPROCAL = 1
+};
+
+/* mhc_sinkhorn_knopp_n4_logits with `flags` (0 or MHC_SK_HW_RECIPROCAL; any
+ * other bit returns MHC_ERR_INVALID_VALUE).  No reference counterpart. */
+MHC_API int mhc_sinkhorn_knopp_n4_logits_ex(const float* d_R, float* d_T, int64_t N, int num_iters, int flags,
+                                            cudaStream_t stream);
+
 /* Gradient with respect to R of sum(G .* sinkhorn_knopp_n4(exp(R))): the
  * backward above times exp(R), in one pass (192 B per matrix instead of
  * 384).  No reference counterpart: it fuses the backward kernel with the

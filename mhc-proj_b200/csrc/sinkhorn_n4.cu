@@ -81,7 +81,9 @@ struct HResInput {
     }
 };
 
-template <bool kVec, class In>
+// kApprox: the factors from the hardware reciprocal (sk_inv_approx) instead
+// of the correctly rounded one.
+template <bool kVec, class In, bool kApprox = false>
 __global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restrict__ T, int64_t N, int iters)
 {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -90,7 +92,7 @@ __global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restri
     in.template load<kVec>(idx, x0);
     Pairs x = to_pairs(x0);
 #pragma unroll 1
-    for (int it = 0; it < iters; ++it) sk_iteration(x, kSkEps, nullptr, nullptr, nullptr);
+    for (int it = 0; it < iters; ++it) sk_iteration<kApprox>(x, kSkEps, nullptr, nullptr, nullptr);
     store_mat<kVec>(T, idx, from_pairs(x));
 }
 
@@ -229,7 +231,7 @@ static void dispatch_sk_bwd(int iters, bool vec, const float* G, const float* M,
     ((iters == Is ? launch_sk_bwd<Is, kLogits>(vec, G, M, D, N, stream) : void()), ...);
 }
 
-template <bool kLogits>
+template <bool kLogits, bool kApprox = false>
 static int sk_forward(const float* d_M, float* d_T, int64_t N, int num_iters, cudaStream_t stream)
 {
     if (N < 0 || (N > 0 && (!d_M || !d_T))) return MHC_ERR_INVALID_VALUE;
@@ -238,9 +240,9 @@ static int sk_forward(const float* d_M, float* d_T, int64_t N, int num_iters, cu
     const int64_t grid = ceil_div(N, kSkBlock);
     using In = std::conditional_t<kLogits, ExpInput, MInput>;
     if (aligned16(d_M) && aligned16(d_T))
-        sk_fwd_kernel<true, In><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
+        sk_fwd_kernel<true, In, kApprox><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
     else
-        sk_fwd_kernel<false, In><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
+        sk_fwd_kernel<false, In, kApprox><<<grid, kSkBlock, 0, stream>>>(In{d_M}, d_T, N, iters);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -295,6 +297,14 @@ extern "C" int mhc_sinkhorn_knopp_n4_logits(const float* d_R, float* d_T, int64_
                                             cudaStream_t stream)
 {
     return sk_forward<true>(d_R, d_T, N, num_iters, stream);
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_logits_ex(const float* d_R, float* d_T, int64_t N, int num_iters, int flags,
+                                               cudaStream_t stream)
+{
+    if (flags & ~MHC_SK_HW_RECIPROCAL) return MHC_ERR_INVALID_VALUE;
+    return (flags & MHC_SK_HW_RECIPROCAL) ? sk_forward<true, true>(d_R, d_T, N, num_iters, stream)
+                                          : sk_forward<true>(d_R, d_T, N, num_iters, stream);
 }
 
 extern "C" int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const float* d_R, float* d_D, int64_t N,

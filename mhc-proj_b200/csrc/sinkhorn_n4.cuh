@@ -46,9 +46,19 @@ __device__ __forceinline__ float rcp_rn(float x)
 }
 
 // The Sinkhorn-Knopp factor: s > eps ? 1/s : 0 with the reciprocal correctly
-// rounded.  Equal to (s > eps) ? __frcp_rn(s) : 0 for all 2^32 s at eps = 1e-8
-// (tests/test_reciprocal_gpu.py).
-__device__ __forceinline__ float sk_inv(float s, float eps) { return (s > eps) ? rcp_rn(s) : 0.0f; }
+// rounded.  For finite s > eps > 0, rcp_rn's guard never fires (e is finite),
+// so the Newton step runs unguarded; s = +inf is clamped to FLT_MAX, whose
+// approximate reciprocal flushes to zero and leaves e = 1, so the factor is
+// 0 = 1/inf there.  Equal to (s > eps) ? __frcp_rn(s) : 0 for all 2^32 s at
+// eps = 1e-8 (tests/test_reciprocal_gpu.py), in one instruction fewer.
+__device__ __forceinline__ float sk_inv(float s, float eps)
+{
+    const float x = fminf(s, 3.40282347e38f);
+    float r0;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(x));
+    const float e = __fmaf_rn(-x, r0, 1.0f);
+    return (s > eps) ? __fmaf_rn(r0, e, r0) : 0.0f;
+}
 
 // The same factor from the hardware reciprocal (rcp.approx.ftz: at most one
 // ulp from 1/s, against the half ulp of __frcp_rn) -- for the backward's
@@ -138,9 +148,12 @@ __device__ __forceinline__ void sk_iteration(Pairs& x, float eps, Pairs* xr_out,
 
 // Reverse of one iteration.  dy holds d/dy on entry and d/dz on exit.
 //   column step  dx_ij = (dy_ij - cs_j cinv_j) cinv_j,  cs_j = sum_k dy_kj x_kj
-//                (an FMA chain over k = 0..3)
+//                (an FMA chain over k = 0..3), formed as
+//                fma(dy_ij, cinv_j, -((cs_j cinv_j) cinv_j)): one packed FMA
+//                per pair of entries instead of an FMA and a multiply
 //   row step     dz_ij = (dx_ij - rs_i) rinv_i,  rs_i = sum_l dx_il x_il
-//                (an FMA chain over l = 0..3)
+//                (an FMA chain over l = 0..3), formed as
+//                fma(dx_ij, rinv_i, -(rs_i rinv_i))
 __device__ __forceinline__ void sk_iteration_vjp(Pairs& dy, const Pairs& xr, const float rinv[4],
                                                  const float cinv[4])
 {
@@ -151,9 +164,10 @@ __device__ __forceinline__ void sk_iteration_vjp(Pairs& dy, const Pairs& xr, con
         cs = __ffma2_rn(dy.p[4 + h], xr.p[4 + h], cs);
         cs = __ffma2_rn(dy.p[6 + h], xr.p[6 + h], cs);
         const float2 ci = make_float2(cinv[2 * h], cinv[2 * h + 1]);
-        const float2 ncs = make_float2(-cs.x, -cs.y);
+        const float2 t = __fmul2_rn(__fmul2_rn(cs, ci), ci);
+        const float2 nt = make_float2(-t.x, -t.y);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dy.p[2 * i + h] = __fmul2_rn(__ffma2_rn(ncs, ci, dy.p[2 * i + h]), ci);
+        for (int i = 0; i < 4; ++i) dy.p[2 * i + h] = __ffma2_rn(dy.p[2 * i + h], ci, nt);
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -163,9 +177,9 @@ __device__ __forceinline__ void sk_iteration_vjp(Pairs& dy, const Pairs& xr, con
         rs = __fmaf_rn(a.y, u.y, rs);
         rs = __fmaf_rn(b.x, w.x, rs);
         rs = __fmaf_rn(b.y, w.y, rs);
-        const float2 nrs = splat(-rs);
-        dy.p[2 * i] = __fmul2_rn(__fadd2_rn(a, nrs), splat(rinv[i]));
-        dy.p[2 * i + 1] = __fmul2_rn(__fadd2_rn(b, nrs), splat(rinv[i]));
+        const float2 nt = splat(-__fmul_rn(rs, rinv[i]));
+        dy.p[2 * i] = __ffma2_rn(a, splat(rinv[i]), nt);
+        dy.p[2 * i + 1] = __ffma2_rn(b, splat(rinv[i]), nt);
     }
 }
 

@@ -256,8 +256,11 @@ py::dict sinkhorn_knopp_n4_backward(torch::Tensor G, torch::Tensor M, int max_it
 
 // Fused exp + Sinkhorn-Knopp on the logits R (no reference counterpart: the
 // reference forms exp(R) in Python, mhc_proj/module.py:50,70).
-py::dict sinkhorn_knopp_n4_logits(torch::Tensor R, int max_iter, const py::kwargs&)
+// approx_reciprocal=True (an optional keyword) takes the hardware reciprocal
+// (MHC_SK_HW_RECIPROCAL): not the reference kernel's bits, within 1e-6 of them.
+py::dict sinkhorn_knopp_n4_logits(torch::Tensor R, int max_iter, const py::kwargs& kwargs)
 {
+    const bool approx = kwargs.contains("approx_reciprocal") && py::cast<bool>(kwargs["approx_reciprocal"]);
     check_batch(R, "R");
     const auto src = R.options();
     const auto opts = target_options(R);
@@ -266,8 +269,8 @@ py::dict sinkhorn_knopp_n4_logits(torch::Tensor R, int max_iter, const py::kwarg
     R = R.contiguous();
     const int64_t n = R.size(0);
     torch::Tensor T = torch::empty({n, 4, 4}, opts);
-    check_status(mhc_sinkhorn_knopp_n4_logits(R.data_ptr<float>(), T.data_ptr<float>(), n, max_iter,
-                                              current_stream()),
+    check_status(mhc_sinkhorn_knopp_n4_logits_ex(R.data_ptr<float>(), T.data_ptr<float>(), n, max_iter,
+                                                 approx ? MHC_SK_HW_RECIPROCAL : 0, current_stream()),
                  "sinkhorn_knopp_n4_logits");
     py::dict out;
     out["T"] = T.to(src);

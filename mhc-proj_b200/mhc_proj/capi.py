@@ -25,6 +25,7 @@ EXPORTED = (
     "mhc_sinkhorn_knopp_n4",
     "mhc_sinkhorn_knopp_n4_backward",
     "mhc_sinkhorn_knopp_n4_logits",
+    "mhc_sinkhorn_knopp_n4_logits_ex",
     "mhc_sinkhorn_knopp_n4_logits_backward",
     "mhc_birkhoff_proj_n4_hres",
     "mhc_birkhoff_proj_n4_hres_backward_workspace",
@@ -44,6 +45,7 @@ MHC_ERR_ITERS = -2
 MHC_ERR_CAPTURE = -3
 MHC_SK_BACKWARD_MAX_ITERS = 20
 MHC_DTYPE_F32, MHC_DTYPE_BF16, MHC_DTYPE_F16 = 0, 1, 2
+MHC_SK_HW_RECIPROCAL = 1
 
 
 class MhcError(RuntimeError):
@@ -73,6 +75,7 @@ def lib() -> ctypes.CDLL:
         L.mhc_birkhoff_proj_n4_duals.argtypes = [vp, vp, vp, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_backward_duals.argtypes = [vp, vp, vp, vp, i64, vp]
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_logits_ex.argtypes = [vp, vp, i64, i32, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
         L.mhc_birkhoff_proj_n4_hres.argtypes = [vp, i64, vp, vp, vp, vp, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_hres_backward_workspace.argtypes = [i64, ctypes.POINTER(i64)]
@@ -153,6 +156,10 @@ def sinkhorn_knopp_n4_backward(G: int, M: int, D: int, N: int, num_iters: int, s
 
 def sinkhorn_knopp_n4_logits(R: int, T: int, N: int, num_iters: int, stream: int = 0) -> None:
     _check(lib().mhc_sinkhorn_knopp_n4_logits(R, T, N, num_iters, stream), "mhc_sinkhorn_knopp_n4_logits")
+
+
+def sinkhorn_knopp_n4_logits_ex(R: int, T: int, N: int, num_iters: int, flags: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_logits_ex(R, T, N, num_iters, flags, stream), "mhc_sinkhorn_knopp_n4_logits_ex")
 
 
 def sinkhorn_knopp_n4_logits_backward(G: int, R: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:

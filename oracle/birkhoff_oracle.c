@@ -18,7 +18,8 @@
  *   - the Sinkhorn-Knopp n4 backward, two versions (sk_backward_one):
  *       * exact: the exact vector-Jacobian product of the forward (what
  *         PyTorch autograd of the same forward gives), with its sums formed
- *         as the left-to-right FMA chains of this repository's kernel;
+ *         as the left-to-right FMA chains of this repository's kernel and
+ *         each step as the kernel's fused multiply-add;
  *       * reference row step: the reference kernel's reverse loop
  *         src/sinkhorn_knopp.cuh:1146-1202 including its row step
  *         (d - r*rinv)*rinv at :1182-1201, which differs from the exact VJP
@@ -350,7 +351,12 @@ static void sk_backward_one(const float G[16], const float M[16], float D[16],
             } else {     /* as the reference's build contracts ((a+b)+c)+d of products */
                 cs = fmaf(dx[12 + j], xr[12 + j], fmaf(dx[8 + j], xr[8 + j], fmaf(dx[j], xr[j], dx[4 + j] * xr[4 + j])));
             }
-            for (int i = 0; i < 4; i++) dx[4 * i + j] = fmaf(-cs, ci[it][j], dx[4 * i + j]) * ci[it][j];
+            if (exact) { /* fma(dy, cinv, -((cs cinv) cinv)), as the kernel forms it */
+                const float t = (cs * ci[it][j]) * ci[it][j];
+                for (int i = 0; i < 4; i++) dx[4 * i + j] = fmaf(dx[4 * i + j], ci[it][j], -t);
+            } else {
+                for (int i = 0; i < 4; i++) dx[4 * i + j] = fmaf(-cs, ci[it][j], dx[4 * i + j]) * ci[it][j];
+            }
         }
         /* row step x = z * rinv: dz = (dx - sum_l dx_il x_il) rinv_i (exact), or
          * the reference's (dx - r rinv) rinv (sinkhorn_knopp.cuh:1182-1201) */
@@ -366,8 +372,13 @@ static void sk_backward_one(const float G[16], const float M[16], float D[16],
             } else {
                 rs = fmaf(d4[3], x4[3], fmaf(d4[2], x4[2], fmaf(d4[0], x4[0], d4[1] * x4[1])));
             }
-            const float sub = exact ? rs : rs * ri[it][i];
-            for (int j = 0; j < 4; j++) dx[4 * i + j] = (dx[4 * i + j] - sub) * ri[it][i];
+            if (exact) { /* fma(dx, rinv, -(rs rinv)), as the kernel forms it */
+                const float t = rs * ri[it][i];
+                for (int j = 0; j < 4; j++) dx[4 * i + j] = fmaf(dx[4 * i + j], ri[it][i], -t);
+            } else {
+                const float sub = rs * ri[it][i];
+                for (int j = 0; j < 4; j++) dx[4 * i + j] = (dx[4 * i + j] - sub) * ri[it][i];
+            }
         }
     }
     memcpy(D, dx, sizeof(dx));

@@ -334,3 +334,43 @@ def test_sinkhorn_against_the_newton_path():
     assert float(diff.max()) < 1e-2
     assert float((Tn.sum(2) - 1).abs().max()) < TOL
     assert float((Ts.sum(1) - 1).abs().max()) < TOL  # SK ends on a column normalisation
+
+
+# --- the Sinkhorn-Knopp forward with the hardware reciprocal (opt-in) -------
+
+@pytest.mark.parametrize("kind,n", [("normal", 4096), ("normal", 1 << 22), ("sigma_mix", 1 << 20), ("wide", 1 << 20)])
+def test_sinkhorn_hw_reciprocal_within_tolerance(kind, n):
+    """MHC_SK_HW_RECIPROCAL: within 1e-6 of the correctly rounded forward (the
+    reference kernel's bits) on every distribution, and within 1e-5 of the
+    vanilla PyTorch Sinkhorn-Knopp (float64) where vanilla's eps semantics
+    agree with the kernel's (N(0,1) logits; at N(0,100) vanilla's eps
+    dominates tiny rows and the two algorithms differ)."""
+    R = make_logits(kind, n, seed=123)
+    s = torch.cuda.current_stream().cuda_stream
+    T = torch.empty_like(R)
+    Ta = torch.empty_like(R)
+    capi.sinkhorn_knopp_n4_logits(R.data_ptr(), T.data_ptr(), n, 20, s)
+    capi.sinkhorn_knopp_n4_logits_ex(R.data_ptr(), Ta.data_ptr(), n, 20, capi.MHC_SK_HW_RECIPROCAL, s)
+    torch.cuda.synchronize()
+    assert float((Ta - T).abs().max()) < 1e-6
+    if kind == "normal":
+        m = min(n, 1 << 16)
+        P = oracle.vanilla_sinkhorn(R[:m].double())
+        assert float((Ta[:m].double() - P).abs().max()) < 1e-5
+
+
+def test_sinkhorn_hw_reciprocal_module_and_flags():
+    import mhc_proj
+
+    x = make_logits("normal", 4096, seed=123).requires_grad_(True)
+    G = make_logits("normal", 4096, seed=124)
+    T0 = mhc_proj.MHCSinkhornN4(20)(x)
+    (T0 * G).sum().backward()
+    g0 = x.grad.clone()
+    x.grad = None
+    T1 = mhc_proj.MHCSinkhornN4(20, approx_reciprocal=True)(x)
+    (T1 * G).sum().backward()
+    assert float((T1 - T0).abs().max()) < 1e-6
+    assert torch.equal(x.grad, g0)  # the backward recomputes from R either way
+    with pytest.raises(capi.MhcError):
+        capi.sinkhorn_knopp_n4_logits_ex(x.data_ptr(), T0.data_ptr(), 4096, 20, 2, 0)

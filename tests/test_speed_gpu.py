@@ -3,10 +3,11 @@ on the same device and the same inputs, CUDA-event timing after warm-up:
   - N = 2^22, x ~ N(0,1) and the training-shaped sigma mix: the Newton
     forward and the IFT backward each at least 1.5x faster;
   - small batches, N = 2^6 ... 2^14 (an mHC layer's decode or micro-batch):
-    forward and forward + backward per call, each call on a fresh input from
-    a pool of 8, within 10% of the reference (the two-lanes-per-matrix kernel
-    below 2^13 measured 0-5% either side of it) and not slower at 2^13 and
-    2^14.
+    forward and forward + backward per call, device time of calls replayed
+    from a CUDA graph (host launch overhead excluded), each call on a fresh
+    input from a pool of 8: within 10% of the reference (the
+    two-lanes-per-matrix kernel below 2^13 measured 0-5% either side of it)
+    and not slower at 2^13 and 2^14.
 The measured times are printed."""
 import pytest
 import torch
@@ -53,18 +54,33 @@ def test_faster_than_reference_kernels(kind):
     assert ref_b / our_b > 1.5
 
 
-def _us_per_call(fn, reps=200):
-    for _ in range(20):
-        fn()
+def _graph_us_per_call(call, calls=20, replays=20):
+    """Device time per call: `calls` calls captured in one CUDA graph (so the
+    host's launch overhead is not timed), the graph replayed `replays` times
+    between CUDA events."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            call(i, s.cuda_stream)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(calls):
+            call(i, s.cuda_stream)
+    for _ in range(3):
+        g.replay()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(reps):
-        fn()
+    for _ in range(replays):
+        g.replay()
     e1.record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) * 1e3 / reps
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (calls * replays)
 
 
 @pytest.mark.parametrize("kind", ["normal", "sigma_mix"])
@@ -72,8 +88,6 @@ def test_small_batches_against_reference_kernels(kind):
     if not oracle.RefCuda.available():
         pytest.skip("reference kernels not built")
     ref = oracle.RefCuda()
-    s = torch.cuda.current_stream().cuda_stream
-    worst = []
     for lg in range(6, 15):
         n = 1 << lg
         Rs = [make_logits(kind, n, seed=100 + i) for i in range(8)]
@@ -81,21 +95,18 @@ def test_small_batches_against_reference_kernels(kind):
         T = torch.empty_like(Rs[0])
         D = torch.empty_like(T)
         for backward in (False, True):
-            def ours(i=[0]):
-                R = Rs[i[0] % 8]
-                i[0] += 1
+            def ours(i, s):
+                R = Rs[i % 8]
                 capi.birkhoff_proj_n4(R.data_ptr(), T.data_ptr(), 1e-6, n, s)
                 if backward:
                     capi.birkhoff_proj_n4_backward(G.data_ptr(), T.data_ptr(), D.data_ptr(), n, s)
 
-            def theirs(i=[0]):
-                R = Rs[i[0] % 8]
-                i[0] += 1
+            def theirs(i, s):
+                R = Rs[i % 8]
                 ref.birkhoff_proj_n4(R.data_ptr(), T.data_ptr(), 1e-6, n, s)
                 if backward:
                     ref.birkhoff_proj_n4_backward(G.data_ptr(), T.data_ptr(), D.data_ptr(), n, s)
 
-            a, b = _us_per_call(ours), _us_per_call(theirs)
-            worst.append((a / b, lg, backward))
+            a, b = _graph_us_per_call(ours), _graph_us_per_call(theirs)
             print(f"\n[{kind} N=2^{lg} {'fwd+bwd' if backward else 'fwd'}] this {a:.1f} us, reference {b:.1f} us")
             assert a <= (1.0 if lg >= 13 else 1.10) * b, (kind, lg, backward, a, b)
