@@ -11,9 +11,13 @@
 
 namespace mhcp {
 
-constexpr int kNewtonBlock = 128;
+// The persistent forward runs one block of 20 warps per SM (96 registers a
+// thread fill the register file), all sharing the SM's slice of the batch.
+constexpr int kFwdWarps = 20;
+constexpr int kNewtonBlock = 32 * kFwdWarps;
+constexpr int kPairBlock = 128;  // the small-batch kernel's block
 // Each forward warp stages its next matrices in a shared-memory ring of
-// kRing slots, kRingHalf at a time (8 KB per warp, 32 KB per block).
+// kRing slots, kRingHalf (one claimed chunk) at a time: 5 KB per warp.
 constexpr int kRingHalf = 32;
 constexpr int kRing = 2 * kRingHalf;
 
@@ -91,12 +95,15 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
     }
 }
 
-// Newton forward, persistent.  Warp w owns matrices [w*per_warp, ...) of the
-// batch.  Each lane runs the reference algorithm (birkhoff_proj_n4.cu:375-499)
-// for one matrix as a state machine, and a lane that finishes stores its T and
-// takes the warp's next matrix, so a warp costs the sum of its matrices' work
-// over 32 instead of the maximum over each group of 32 (per-matrix work ranges
-// from 4 to ~140 evaluations).
+// Newton forward, persistent.  Block b (one per SM) owns matrices
+// [b*per_block, ...) of the batch, and its 20 warps take them 32 at a time:
+// warp w's first chunk is the w-th, later ones come from a shared counter, so
+// the warps of an SM run out of work together instead of each at the end of a
+// fixed slice of its own.  Each lane runs the reference algorithm
+// (birkhoff_proj_n4.cu:375-499) for one matrix as a state machine, and a lane
+// that finishes stores its T and takes the warp's next matrix, so a warp costs
+// the sum of its matrices' work over 32 instead of the maximum over each group
+// of 32 (per-matrix work ranges from 4 to ~140 evaluations).
 //
 // Every step is the same straight-line code for every lane: one log-sum-exp
 // pass whose lines are rows or columns as the stage needs, the row and the
@@ -120,20 +127,20 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // instead of as two steps of the state machine).  A refill -- which a few
 // lanes of the warp take each step -- is then five predicated shared-memory
 // loads (R and the starting beta) instead of global loads and arithmetic
-// issued for those few lanes.  The bound of 5 blocks per SM keeps the
-// register count at the 5-block occupancy (96 registers) that the ring's
-// addressing would otherwise push past.
+// issued for those few lanes.  The launch bound (640 threads, one block per
+// SM) caps the registers at the 96 that 20 resident warps allow.
 //
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
 // kStats: also write, per matrix, the number of Newton iterations taken and
 // the final gradient l1 norm, and, when `counts` is given, add the warp's
-// pass counts by stage to it (MHC_PASS_* in mhc_proj.h); kDuals: also write the final beta (4 floats,
-// the point whose T is the output: T = row-softmax(beta + R)).  Separate
-// instantiations; the plain one carries no cost for either.
+// pass counts by stage to it (MHC_PASS_* in mhc_proj.h); kDuals: also write
+// the final beta (4 floats, the point whose T is the output: T =
+// row-softmax(beta + R)).  Separate instantiations; the plain one carries no
+// cost for either.
 template <class Rd, class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
-__global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
-                                                                    int64_t N, int64_t per_warp,
+__global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
+                                                                    int64_t N, int64_t per_block,
                                                                     int32_t* __restrict__ iters_out = nullptr,
                                                                     float* __restrict__ gnorm_out = nullptr,
                                                                     float* __restrict__ beta_out = nullptr,
@@ -141,12 +148,19 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
 {
     using Prod = typename Rd::P;
     const int lane = threadIdx.x & 31;
-    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t begin = warp * per_warp;
-    if (begin >= N) return;  // warp-uniform
-    // The warp's slice, addressed by 32-bit offsets from its first matrix
-    // (per_warp is at most ceil(N / warps) and far below 2^31).
-    const int cnt = static_cast<int>(min(N - begin, per_warp));
+    const int64_t begin = static_cast<int64_t>(blockIdx.x) * per_block;
+    if (begin >= N) return;  // block-uniform
+    // The block's slice, addressed by 32-bit offsets from its first matrix
+    // (per_block is at most ceil(N / blocks) and below 2^31).  Its warps take
+    // 32 matrices at a time from it through a shared counter.
+    const int blk_cnt = static_cast<int>(min(N - begin, per_block));
+    // Warp w's first chunk is the w-th (so that the warps holding a small
+    // pool's matrices sit on different SM sub-partitions); later chunks are
+    // claimed through the shared counter.
+    __shared__ int pool_next;
+    if (threadIdx.x == 0) pool_next = 32 * kFwdWarps;
+    __syncthreads();
+    int cnt = 0;  // matrices this warp has claimed (positions [0, cnt) of its sequence)
     src.advance(begin);
     Tout += begin * 16;
     if constexpr (kStats) {
@@ -161,13 +175,17 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     float beta[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     int k = 0, it = 0;
-    int idx = lane;  // offset in the warp's slice
+    int idx = 0;  // the lane's matrix, offset in the block's slice
     int stage = kIdle;
     // A ring slot is five 16-byte entries: the four rows of R and the
     // starting beta.  One more entry per warp after the ring holds the warp's
     // output pointer (below).
     constexpr int kSlot = 5;
-    __shared__ float4 ring_all[kNewtonBlock / 32][kRing * kSlot + 1];
+    extern __shared__ float4 ring_dyn[];
+    float4 (*ring_all)[kRing * kSlot + 1] = reinterpret_cast<float4 (*)[kRing * kSlot + 1]>(ring_dyn);
+    // the block offsets of the two chunks in the warp's ring
+    __shared__ int chunk_all[kNewtonBlock / 32][2];
+    int* chunk = chunk_all[threadIdx.x >> 5];
     // The line-search steps gamma_k as a per-warp table: one shared load per
     // step instead of a chain of compares and selects.
     __shared__ float gtab_all[kNewtonBlock / 32][8];
@@ -194,13 +212,20 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
                      : "r"(static_cast<unsigned>(__cvta_generic_to_shared(ring + kRing * kSlot))));
         return v;
     };
-    auto fill = [&](int first) {  // matrices [first, first + kRingHalf) into their slots
-#pragma unroll 1
-        for (int u = 0; u < kRingHalf / 32; ++u) {
-            const int i = first + 32 * u + lane;
-            if (i < cnt) {
+    auto fill = [&](int first) {  // the next 32 matrices of the pool into positions [first, first + 32)
+        int c = 32 * static_cast<int>(threadIdx.x >> 5);
+        if (first > 0) {
+            if (lane == 0) c = atomicAdd(&pool_next, 32);
+            c = __shfl_sync(kFullMask, c, 0);
+        }
+        const int valid = max(0, min(32, blk_cnt - c));
+        if (lane == 0) chunk[(first >> 5) & 1] = c;
+        cnt += valid;
+        {
+            const int i = first + lane;
+            if (lane < valid) {
                 Mat4 m;
-                src.load(i, m);
+                src.load(c + lane, m);
                 float b[4];
                 start_point(m.m, b);
                 float4* slot = ring + (i & (kRing - 1)) * kSlot;
@@ -231,9 +256,10 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     fill(0);
     fill(kRingHalf);
     __syncwarp();
-    int base = 0;  // the ring holds matrices [base, base + kRing)
-    take_if(idx < cnt, idx);
-    if (idx < cnt) stage = kStart;
+    int base = 0;  // the ring holds positions [base, base + kRing)
+    take_if(lane < cnt, lane);
+    if (lane < cnt) stage = kStart;
+    idx = chunk[0] + lane;
     int next = min(cnt, 32);
     // kStats with counts: the warp's pass counts, the same in every lane
     unsigned tally[MHC_PASS_COUNTERS] = {};
@@ -351,7 +377,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
         const unsigned want = __ballot_sync(kFullMask, done);
         const int cand = next + __popc(want & ((1u << lane) - 1u));
         const bool get = done && cand < cnt;
-        idx = sel(done, cand, idx);
+        idx = sel(get, chunk[(cand >> 5) & 1] + (cand & 31), idx);
         take_if(get, cand);
         stage = sel(get, static_cast<int>(kStart), stage);
         next = min(cnt, next + __popc(want));
@@ -365,7 +391,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
     if constexpr (kStats) {
         if (counts && lane == 0) {
             tally[MHC_PASS_MATRICES] = static_cast<unsigned>(cnt);
-            tally[MHC_PASS_FILL] = 2u * static_cast<unsigned>(cnt);
+            tally[MHC_PASS_FILL] = 2u * static_cast<unsigned>(cnt);  // this warp's claimed matrices
             for (int q = 0; q < MHC_PASS_COUNTERS; ++q)
                 if (tally[q]) atomicAdd(counts + q, static_cast<unsigned long long>(tally[q]));
         }
@@ -385,7 +411,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 5) birkhoff_fwd_kernel(Src src, 
 // state machine is the persistent kernel's without the ring: each pair owns
 // one matrix, which it stores (its two rows each) when it finishes.
 template <class Rd, class Src, class Elem, bool kVec>
-__global__ void __launch_bounds__(kNewtonBlock) birkhoff_fwd_pair_kernel(Src src, Elem* __restrict__ Tout, float tol,
+__global__ void __launch_bounds__(kPairBlock) birkhoff_fwd_pair_kernel(Src src, Elem* __restrict__ Tout, float tol,
                                                                          int64_t N)
 {
     const int64_t m = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 1;
@@ -605,13 +631,16 @@ __global__ void __launch_bounds__(kHResBlock) birkhoff_hres_bwd_kernel(
     block_partial_sums<kHResBlock>(acc, partials, gridDim.x, blockIdx.x);
 }
 
-// Resident warps of a forward kernel instantiation on the current device,
+// Resident blocks of a forward kernel instantiation on the current device,
 // queried once per device and instantiation (so later launches make no extra
 // runtime calls, which also keeps them legal inside stream capture).
 constexpr int kMaxDevices = 64;
+// Dynamic shared memory of a forward block: each warp's ring (64 slots of
+// five 16-byte entries) and its output pointer.
+constexpr int kFwdRingBytes = kFwdWarps * (kRing * 5 + 1) * 16;
 
 template <auto kKernel>
-static int64_t forward_warp_slots()
+static int64_t forward_block_slots()
 {
     static std::atomic<int64_t> cache[kMaxDevices];  // per instantiation; 0 = not queried yet
     int dev = 0;
@@ -622,9 +651,12 @@ static int64_t forward_warp_slots()
     }
     int sms = 0, blocks = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, kNewtonBlock, 0) != cudaSuccess || blocks < 1)
+    if (cudaFuncSetAttribute(kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdRingBytes) != cudaSuccess)
         return 0;
-    const int64_t slots = static_cast<int64_t>(sms) * blocks * (kNewtonBlock / 32);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, kNewtonBlock, kFwdRingBytes) != cudaSuccess ||
+        blocks < 1)
+        return 0;
+    const int64_t slots = static_cast<int64_t>(sms) * blocks;  // resident blocks
     if (dev >= 0 && dev < kMaxDevices) cache[dev].store(slots, std::memory_order_relaxed);
     return slots;
 }
@@ -634,19 +666,18 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
                           float* gnorm = nullptr, float* beta = nullptr, unsigned long long* counts = nullptr)
 {
     constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats, kDuals>;
-    const int64_t slots = forward_warp_slots<kernel>();
+    const int64_t slots = forward_block_slots<kernel>();
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
         return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
     }
-    // Enough warps to fill the GPU once; each takes an equal contiguous share,
-    // small enough for the kernel's 32-bit offsets within a share.
-    const int64_t warps = max(min(ceil_div(N, 32), slots), ceil_div(N, int64_t{1} << 30));
-    const int64_t per_warp = ceil_div(N, warps);
-    const int64_t used = ceil_div(N, per_warp);
-    const int64_t grid = ceil_div(used * 32, kNewtonBlock);
-    kernel<<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N, per_warp, iters, gnorm, beta,
-                                              counts);
+    // Enough blocks to fill the GPU once, each an equal contiguous share that
+    // its warps take 32 matrices at a time, small enough for 32-bit offsets.
+    const int64_t blocks = max(min(ceil_div(N, 32), slots), ceil_div(N, int64_t{1} << 30));
+    const int64_t per_block = ceil_div(N, blocks);
+    const int64_t grid = ceil_div(N, per_block);
+    kernel<<<grid, kNewtonBlock, kFwdRingBytes, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters,
+                                                          gnorm, beta, counts);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -659,9 +690,9 @@ constexpr int64_t kPairMaxN = MHC_PAIR_MAX_N;
 template <class Src, class Elem, bool kVec>
 static int launch_forward_pairs(Src src, void* T, float tol, int64_t N, cudaStream_t stream)
 {
-    const int64_t grid = ceil_div(2 * N, kNewtonBlock);
+    const int64_t grid = ceil_div(2 * N, kPairBlock);
     birkhoff_fwd_pair_kernel<RefRounding, Src, Elem, kVec>
-        <<<grid, kNewtonBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N);
+        <<<grid, kPairBlock, 0, stream>>>(src, static_cast<Elem*>(T), tol, N);
     return static_cast<int>(cudaGetLastError());
 }
 
