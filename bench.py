@@ -364,7 +364,7 @@ def run_ours(args):
     # end to end through the public API with host buffers: pinned inputs go
     # up, T and D come back, chunks pipelined over two streams
     e2e = run_e2e(args, R, G, dev, world) if args.workload == "newton" else {"ms": float("nan"), "h2d": 0, "d2h": 0, "how": "not measured for this workload"}
-    ceiling_ms = copy_ceiling_ms(args, R, dev, world) if args.workload == "newton" else float("nan")
+    ceiling_ms = e2e.get("ceiling_ms", float("nan"))
     passes = forward_passes(R, tol) if args.workload == "newton" and rank == 0 else None
     bwd_cold_ms = backward_cold_l2_ms(bwd, fwd, dev) if args.workload == "newton" else float("nan")
     unfused_ms = sinkhorn_unfused_ms(R, G, args.steps) if args.workload == "sinkhorn" else None
@@ -777,55 +777,15 @@ def sharded_mixture(args, dev, world, rank):
             "per_gpu": per_gpu}
 
 
-def copy_ceiling_ms(args, R, dev, world):
-    """Per-step device time of run_e2e's host<->device copies alone (same
-    chunks, streams and pinned buffers, no kernels), on every rank at once."""
-    import torch
-
-    n = R.shape[0]
-    chunks = 16 if n >= (1 << 20) else 1
-    Rh = torch.empty((n, 4, 4), dtype=R.dtype).pin_memory()
-    Gh = torch.empty_like(Rh).pin_memory()
-    Th = torch.empty_like(Rh).pin_memory()
-    Dh = torch.empty_like(Rh).pin_memory()
-    Rd = torch.empty_like(R)
-    Gd = torch.empty_like(R)
-    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
-    bounds = [(n * i // chunks, n * (i + 1) // chunks) for i in range(chunks)]
-
-    def step():
-        for i, (a, b) in enumerate(bounds):
-            s = streams[i % len(streams)]
-            with torch.cuda.stream(s):
-                Rd[a:b].copy_(Rh[a:b], non_blocking=True)
-                Gd[a:b].copy_(Gh[a:b], non_blocking=True)
-                Th[a:b].copy_(Rd[a:b], non_blocking=True)
-                Dh[a:b].copy_(Gd[a:b], non_blocking=True)
-        for s in streams:
-            torch.cuda.current_stream(dev).wait_stream(s)
-
-    step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier(device_ids=[dev.index])
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.e2e_steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    return e0.elapsed_time(e1) / args.e2e_steps
-
-
 def run_e2e(args, R, G, dev, world):
     """End to end through mhc_proj.torch.* with host buffers: each step copies
     R and G from pinned host memory, runs the forward and backward, and copies
     T and D back to pinned host memory; the batch moves in chunks over three
-    streams so copies in both directions overlap the kernels."""
+    streams so copies in both directions overlap the kernels.  Then the copy
+    ceiling: the same copies (same chunks, streams and pinned buffers) on every
+    rank at once with no kernels."""
     import torch
+    import torch.distributed as dist
 
     import mhc_proj
 
@@ -858,8 +818,6 @@ def run_e2e(args, R, G, dev, world):
         step()
     torch.cuda.synchronize(dev)
     if world > 1:
-        import torch.distributed as dist
-
         dist.barrier(device_ids=[dev.index])
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -869,8 +827,34 @@ def run_e2e(args, R, G, dev, world):
     e1.record()
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / args.e2e_steps
+
+    Rd = torch.empty_like(R)
+    Gd = torch.empty_like(R)
+
+    def copies():
+        for i, (a, b) in enumerate(bounds):
+            s = streams[i % len(streams)]
+            with torch.cuda.stream(s):
+                Rd[a:b].copy_(Rh[a:b], non_blocking=True)
+                Gd[a:b].copy_(Gh[a:b], non_blocking=True)
+                Th[a:b].copy_(Rd[a:b], non_blocking=True)
+                Dh[a:b].copy_(Gd[a:b], non_blocking=True)
+        for s in streams:
+            torch.cuda.current_stream(dev).wait_stream(s)
+
+    copies()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    e0.record()
+    for _ in range(args.e2e_steps):
+        copies()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ceiling_ms = e0.elapsed_time(e1) / args.e2e_steps
+    del Rd, Gd
     nbytes = n * 64
-    return {"ms": ms, "h2d": 2 * nbytes, "d2h": 2 * nbytes,
+    return {"ms": ms, "ceiling_ms": ceiling_ms, "h2d": 2 * nbytes, "d2h": 2 * nbytes,
             "how": f"pinned host R,G -> device -> fwd+bwd (public API) -> T,D to pinned host; "
                    f"{chunks} chunks over {len(streams)} streams; {args.e2e_steps} steps timed with CUDA events"}
 
