@@ -39,8 +39,8 @@ enum Stage : int {
     kIdle = 4,
 };
 
-// Where the forward finds matrix k's logits.  `advance` moves to a warp's
-// first matrix; `load` reads matrix i of the warp's slice (a 32-bit offset).
+// Where the forward finds matrix k's logits.  `advance` moves to a block's
+// first matrix; `load` reads matrix i of the block's slice (a 32-bit offset).
 //
 // DenseSource: R[k] at R + k * stride, stored as Elem.
 template <class Elem, bool kVec>
@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, 
     // One output pointer of the warp lives in shared memory at a fixed offset
     // from the ring instead of in two registers, and is loaded where it is
     // stored through: beta's for kDuals (as two more registers it made that
-    // instantiation spill at the 96-register cap of 5 blocks per SM: 3.31 ms
+    // instantiation spill at the 96-register cap of 20 warps per SM: 3.31 ms
     // at 2^24 instead of 3.17), T's otherwise (3.08 -> 3.05 ms).  The fills'
     // __syncwarp below orders this store before every lane's load.
     if (lane == 0) {
