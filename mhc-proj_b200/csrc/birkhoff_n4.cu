@@ -678,7 +678,17 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     const int64_t grid = ceil_div(N, per_block);
     kernel<<<grid, kNewtonBlock, kFwdRingBytes, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters,
                                                           gnorm, beta, counts);
-    return static_cast<int>(cudaGetLastError());
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaErrorInvalidValue &&
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdRingBytes) == cudaSuccess) {
+        // The shared-memory attribute belongs to the CUDA context: after a
+        // device reset the cached launch shape is still right but the
+        // attribute is gone, so set it again and launch once more.
+        kernel<<<grid, kNewtonBlock, kFwdRingBytes, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters,
+                                                              gnorm, beta, counts);
+        e = cudaGetLastError();
+    }
+    return static_cast<int>(e);
 }
 
 // Batches up to this many matrices take the two-lanes-per-matrix kernel.
