@@ -11,9 +11,11 @@
 
 namespace mhcp {
 
-// The persistent forward runs one block of 20 warps per SM (96 registers a
-// thread fill the register file), all sharing the SM's slice of the batch.
-constexpr int kFwdWarps = 20;
+// The persistent forward runs one block of 22 warps per SM, all sharing the
+// SM's slice of the batch: 80 registers a thread, as six warps share an SM
+// sub-partition's 16K registers (20 warps at 96 registers, or 21 or 24 at 80,
+// measured slower at 2^24 matrices).
+constexpr int kFwdWarps = 22;
 constexpr int kNewtonBlock = 32 * kFwdWarps;
 constexpr int kPairBlock = 128;  // the small-batch kernel's block
 // Each forward warp stages its next matrices in a shared-memory ring of
@@ -96,7 +98,7 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 }
 
 // Newton forward, persistent.  Block b (one per SM) owns matrices
-// [b*per_block, ...) of the batch, and its 20 warps take them 32 at a time:
+// [b*per_block, ...) of the batch, and its 22 warps take them 32 at a time:
 // warp w's first chunk is the w-th, later ones come from a shared counter, so
 // the warps of an SM run out of work together instead of each at the end of a
 // fixed slice of its own.  Each lane runs the reference algorithm
@@ -127,8 +129,8 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // instead of as two steps of the state machine).  A refill -- which a few
 // lanes of the warp take each step -- is then five predicated shared-memory
 // loads (R and the starting beta) instead of global loads and arithmetic
-// issued for those few lanes.  The launch bound (640 threads, one block per
-// SM) caps the registers at the 96 that 20 resident warps allow.
+// issued for those few lanes.  The launch bound (704 threads, one block per
+// SM) caps the registers at the 80 that 22 resident warps allow.
 //
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
@@ -196,8 +198,8 @@ __global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, 
     // One output pointer of the warp lives in shared memory at a fixed offset
     // from the ring instead of in two registers, and is loaded where it is
     // stored through: beta's for kDuals (as two more registers it made that
-    // instantiation spill at the 96-register cap of 20 warps per SM: 3.31 ms
-    // at 2^24 instead of 3.17), T's otherwise (3.08 -> 3.05 ms).  The fills'
+    // instantiation spill at a 96-register cap: 3.31 ms at 2^24 instead of
+    // 3.17), T's otherwise (3.08 -> 3.05 ms).  The fills'
     // __syncwarp below orders this store before every lane's load.
     if (lane == 0) {
         if constexpr (kDuals)
