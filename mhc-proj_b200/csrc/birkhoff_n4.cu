@@ -494,7 +494,8 @@ __global__ void __launch_bounds__(kPairBlock) birkhoff_fwd_pair_kernel(Src src, 
         float cn[3];
 #pragma unroll
         for (int j = 0; j < 3; ++j) cn[j] = half_sum(__fadd_rn(t[j], t[4 + j]));
-        const float fn = -psum4(lse[0], lse[1], lse[2], lse[3]) - psum4(v[0], v[1], v[2], v[3]);
+        // (l0 + l1) + (l2 + l3) from one exchange of the pair's half sums
+        const float fn = -half_sum(__fadd_rn(ls[0], ls[1])) - psum4(v[0], v[1], v[2], v[3]);
         const float gnn = __fadd_rn(__fadd_rn(fabsf(cn[0] - 1.0f), fabsf(cn[1] - 1.0f)), fabsf(cn[2] - 1.0f));
         float pn[6];
         {
