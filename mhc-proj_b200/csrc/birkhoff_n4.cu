@@ -18,6 +18,11 @@ namespace mhcp {
 constexpr int kFwdWarps = 22;
 constexpr int kNewtonBlock = 32 * kFwdWarps;
 constexpr int kPairBlock = 128;  // the small-batch kernel's block
+// Batches up to this many matrices take the two-lanes-per-matrix kernels.
+#ifndef MHC_PAIR_MAX_N
+#define MHC_PAIR_MAX_N (int64_t{1} << 13)
+#endif
+constexpr int64_t kPairMaxN = MHC_PAIR_MAX_N;
 // Each forward warp stages its next matrices in a shared-memory ring of
 // kRing slots, kRingHalf (one claimed chunk) at a time: 5 KB per warp.
 constexpr int kRingHalf = 32;
@@ -600,6 +605,74 @@ __global__ void __launch_bounds__(kBackwardBlock) birkhoff_bwd_kernel(const GE* 
     store_elems<GE, kVec>(D, idx * 16, d);
 }
 
+// The IFT backward of a small batch with two lanes per matrix, as the
+// small-batch forward: lane h takes rows 2h and 2h+1, and every sum over the
+// four rows (the column sums of G.*T and of T, T^T mu_r, the Gram sums) is
+// exchanged as two half sums in the reference's order (r0 + r1) + (r2 + r3);
+// both lanes then solve the same 3x3 system and write their two rows of D.
+// The same bits as birkhoff_bwd_kernel, which leaves a batch that is a
+// fraction of one wave waiting on one thread's whole chain per matrix.
+template <class GE, class TE, bool kVec>
+__global__ void __launch_bounds__(kPairBlock) birkhoff_bwd_pair_kernel(const GE* __restrict__ G, int64_t g_stride,
+                                                                       const TE* __restrict__ T, int64_t t_stride,
+                                                                       GE* __restrict__ D, int64_t N)
+{
+    const int64_t m = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 1;
+    const bool h = (threadIdx.x & 1) != 0;
+    if (m >= N) return;  // both lanes of a pair leave together
+    float g[8], t[8];    // this lane's two rows
+    {
+        Mat4 gm, tm;
+        load_elems<GE, kVec>(G, m * g_stride, gm);
+        load_elems<TE, kVec>(T, m * t_stride, tm);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            g[q] = sel(h, gm.m[8 + q], gm.m[q]);
+            t[q] = sel(h, tm.m[8 + q], tm.m[q]);
+        }
+    }
+    const unsigned pair = 3u << (threadIdx.x & 30);
+    auto half_sum = [&](float mine) { return __fadd_rn(mine, __shfl_xor_sync(pair, mine, 1)); };
+    float mr[2];
+#pragma unroll
+    for (int l = 0; l < 2; ++l)
+        mr[l] = psum4(__fmul_rn(g[4 * l], t[4 * l]), __fmul_rn(g[4 * l + 1], t[4 * l + 1]),
+                      __fmul_rn(g[4 * l + 2], t[4 * l + 2]), __fmul_rn(g[4 * l + 3], t[4 * l + 3]));
+    float rhs[3], c[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        const float muc = half_sum(__fadd_rn(__fmul_rn(g[j], t[j]), __fmul_rn(g[4 + j], t[4 + j])));
+        const float tmu = half_sum(__fadd_rn(__fmul_rn(t[j], mr[0]), __fmul_rn(t[4 + j], mr[1])));
+        rhs[j] = __fsub_rn(muc, tmu);
+        c[j] = half_sum(__fadd_rn(t[j], t[4 + j]));
+    }
+    float p[6];
+    {
+        constexpr int J[6] = {0, 1, 2, 0, 1, 2};
+        constexpr int K[6] = {0, 1, 2, 1, 2, 0};
+#pragma unroll
+        for (int q = 0; q < 6; ++q)
+            p[q] = half_sum(__fadd_rn(__fmul_rn(t[J[q]], t[K[q]]), __fmul_rn(t[4 + J[q]], t[4 + K[q]])));
+    }
+    const Sym3 hm = gram_matrix(p, c, 0.0f);
+    const float det = fmaxf(RefRounding::A::det(hm), kEpsilon);
+    float y0, y1, y2;
+    RefRounding::A::adj(hm, rhs[0], rhs[1], rhs[2], y0, y1, y2);
+    const float rdet = fast_rcp(det);
+    const float w[4] = {__fmul_rn(y0, rdet), __fmul_rn(y1, rdet), __fmul_rn(y2, rdet), 0.0f};
+    float d[8];
+#pragma unroll
+    for (int l = 0; l < 2; ++l) {
+        const float* tr = t + 4 * l;
+        const float tw = psum4(__fmul_rn(tr[0], w[0]), __fmul_rn(tr[1], w[1]), __fmul_rn(tr[2], w[2]),
+                               __fmul_rn(tr[3], w[3]));
+        const float v = __fsub_rn(mr[l], tw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[4 * l + j] = -__fmul_rn(__fsub_rn(__fadd_rn(v, w[j]), g[4 * l + j]), tr[j]);
+    }
+    store_rows2<GE, kVec>(D + m * 16 + (h ? 8 : 0), d);
+}
+
 // The H_res backward: the IFT gradient D = dL/dR of each matrix, carried
 // through R = alpha * h / rms + b.  Per matrix, dh = D * (alpha / rms) and
 // drms = -(alpha / rms^2) * sum(D .* h); over the batch, dalpha =
@@ -694,11 +767,6 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     return static_cast<int>(e);
 }
 
-// Batches up to this many matrices take the two-lanes-per-matrix kernel.
-#ifndef MHC_PAIR_MAX_N
-#define MHC_PAIR_MAX_N (int64_t{1} << 13)
-#endif
-constexpr int64_t kPairMaxN = MHC_PAIR_MAX_N;
 
 template <class Src, class Elem, bool kVec>
 static int launch_forward_pairs(Src src, void* T, float tol, int64_t N, cudaStream_t stream)
@@ -730,6 +798,14 @@ static int backward_typed(const void* G, int64_t g_stride, const void* T, int64_
     const GE* g = static_cast<const GE*>(G);
     const TE* t = static_cast<const TE*>(T);
     GE* d = static_cast<GE*>(D);
+    if (N <= kPairMaxN) {  // two lanes per matrix, as the small-batch forward
+        const int64_t pgrid = ceil_div(2 * N, kPairBlock);
+        if (vec)
+            birkhoff_bwd_pair_kernel<GE, TE, true><<<pgrid, kPairBlock, 0, stream>>>(g, g_stride, t, t_stride, d, N);
+        else
+            birkhoff_bwd_pair_kernel<GE, TE, false><<<pgrid, kPairBlock, 0, stream>>>(g, g_stride, t, t_stride, d, N);
+        return static_cast<int>(cudaGetLastError());
+    }
     if (vec)
         birkhoff_bwd_kernel<RefRounding, GE, TE, true><<<grid, kBackwardBlock, 0, stream>>>(g, g_stride, t, t_stride,
                                                                                             d, N);

@@ -69,3 +69,52 @@ def test_nonfinite_small_batch():
     R[13, 2, 1] = -0.0
     T = capi.birkhoff_proj_n4_tensor(R)
     assert same_bits(T, persistent(R, 1e-6))
+
+
+# --- the small-batch backward (two lanes per matrix up to the same threshold) --
+
+def backward(G, T):
+    D = torch.empty_like(G)
+    capi.birkhoff_proj_n4_backward(G.data_ptr(), T.data_ptr(), D.data_ptr(), G.shape[0],
+                                   torch.cuda.current_stream().cuda_stream)
+    return D
+
+
+@pytest.mark.parametrize("kind", ["normal", "sigma_mix", "wide"])
+@pytest.mark.parametrize("n", [1, 2, 17, 1000, PAIR_MAX_N])
+def test_small_backward_bitwise(kind, n):
+    """Against the reference kernel, and against the one-thread-per-matrix
+    kernel (the same matrices padded past the threshold)."""
+    R = make_logits(kind, n, seed=n + 7)
+    G = make_logits("normal", n, seed=n + 8)
+    T = capi.birkhoff_proj_n4_tensor(R)
+    D = backward(G, T)
+    pad = PAIR_MAX_N + 1
+    Gp = torch.cat([G, make_logits("normal", pad, seed=1)])
+    Tp = torch.cat([T, capi.birkhoff_proj_n4_tensor(make_logits(kind, pad, seed=2))])
+    assert same_bits(D, backward(Gp, Tp)[:n])
+    if oracle.RefCuda.available():
+        ref = oracle.RefCuda()
+        Dr = torch.empty_like(G)
+        ref.birkhoff_proj_n4_backward(G.data_ptr(), T.data_ptr(), Dr.data_ptr(), n,
+                                      torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert same_bits(D, Dr)
+
+
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("tdt", [torch.float32, torch.bfloat16])
+def test_small_backward_native_types(gdt, tdt):
+    n = 3001
+    R = make_logits("sigma_mix", n, seed=5)
+    T32 = capi.birkhoff_proj_n4_tensor(R)
+    G32 = make_logits("normal", n, seed=6)
+    Tb = torch.empty(n * 24 + 16, device="cuda", dtype=tdt)
+    T = torch.as_strided(Tb, (n, 4, 4), (24, 4, 1), 8)
+    T.copy_(T32.to(tdt))
+    Gb = torch.empty(n * 20 + 16, device="cuda", dtype=gdt)
+    G = torch.as_strided(Gb, (n, 4, 4), (20, 4, 1), 4)
+    G.copy_(G32.to(gdt))
+    D = mhc_proj.torch.birkhoff_proj_n4_backward(G, T)["D"]
+    expected = backward(G.float().contiguous(), T.float().contiguous()).to(gdt)
+    assert D.dtype == gdt and same_bits(D, expected)

@@ -5,9 +5,9 @@ on the same device and the same inputs, CUDA-event timing after warm-up:
   - small batches, N = 2^6 ... 2^14 (an mHC layer's decode or micro-batch):
     forward and forward + backward per call, device time of calls replayed
     from a CUDA graph (host launch overhead excluded), each call on a fresh
-    input from a pool of 8: within 10% of the reference (the
-    two-lanes-per-matrix kernel below 2^13 measured 0-5% either side of it)
-    and not slower at 2^13 and 2^14.
+    input from a pool of 8: within 5% of the reference (the
+    two-lanes-per-matrix kernels below 2^13 measured from 4% faster to 1%
+    slower than it) and not slower at 2^13 and 2^14.
 The measured times are printed."""
 import pytest
 import torch
@@ -109,4 +109,4 @@ def test_small_batches_against_reference_kernels(kind):
 
             a, b = _graph_us_per_call(ours), _graph_us_per_call(theirs)
             print(f"\n[{kind} N=2^{lg} {'fwd+bwd' if backward else 'fwd'}] this {a:.1f} us, reference {b:.1f} us")
-            assert a <= (1.0 if lg >= 13 else 1.10) * b, (kind, lg, backward, a, b)
+            assert a <= (1.0 if lg >= 13 else 1.05) * b, (kind, lg, backward, a, b)
