@@ -11,12 +11,16 @@
 
 namespace mhcp {
 
-// The persistent forward runs one block of 22 warps per SM, all sharing the
-// SM's slice of the batch: 80 registers a thread, as six warps share an SM
-// sub-partition's 16K registers (20 warps at 96 registers, or 21 or 24 at 80,
-// measured slower at 2^24 matrices).
-constexpr int kFwdWarps = 22;
-constexpr int kNewtonBlock = 32 * kFwdWarps;
+// The persistent forward runs one block per SM whose warps share the SM's
+// slice of the batch: 20 warps at 96 registers a thread for batches whose
+// steps are still latency-bound, 22 at 80 for the largest (six warps then
+// share an SM sub-partition's 16K registers; 21 or 24 warps were slower).
+constexpr int kFwdWarpsLatency = 20;
+constexpr int kFwdWarpsThroughput = 22;
+#ifndef MHC_FWD_WIDE_N
+#define MHC_FWD_WIDE_N (int64_t{1} << 21)
+#endif
+constexpr int64_t kFwdWideN = MHC_FWD_WIDE_N;  // larger batches take the 22-warp block
 constexpr int kPairBlock = 128;  // the small-batch kernel's block
 // Batches up to this many matrices take the two-lanes-per-matrix kernels.
 #ifndef MHC_PAIR_MAX_N
@@ -103,7 +107,7 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 }
 
 // Newton forward, persistent.  Block b (one per SM) owns matrices
-// [b*per_block, ...) of the batch, and its 22 warps take them 32 at a time:
+// [b*per_block, ...) of the batch, and its kWarps warps take them 32 at a time:
 // warp w's first chunk is the w-th, later ones come from a shared counter, so
 // the warps of an SM run out of work together instead of each at the end of a
 // fixed slice of its own.  Each lane runs the reference algorithm
@@ -134,8 +138,9 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // instead of as two steps of the state machine).  A refill -- which a few
 // lanes of the warp take each step -- is then five predicated shared-memory
 // loads (R and the starting beta) instead of global loads and arithmetic
-// issued for those few lanes.  The launch bound (704 threads, one block per
-// SM) caps the registers at the 80 that 22 resident warps allow.
+// issued for those few lanes.  The launch bound (32 * kWarps threads, one
+// block per SM) caps the registers at what kWarps resident warps allow: 96
+// for 20, 80 for 22.
 //
 // Src supplies the logits (DenseSource or HResSource); Elem is the storage
 // type of T (fp32, bf16 or fp16; computation is fp32), which is contiguous.
@@ -145,8 +150,8 @@ __device__ __forceinline__ void store_vec4_if(bool pred, float* p, const float (
 // the final beta (4 floats, the point whose T is the output: T =
 // row-softmax(beta + R)).  Separate instantiations; the plain one carries no
 // cost for either.
-template <class Rd, class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
-__global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
+template <class Rd, class Src, class Elem, bool kVec, bool kStats, bool kDuals, int kWarps>
+__global__ void __launch_bounds__(32 * kWarps, 1) birkhoff_fwd_kernel(Src src, Elem* __restrict__ Tout, float tol,
                                                                     int64_t N, int64_t per_block,
                                                                     int32_t* __restrict__ iters_out = nullptr,
                                                                     float* __restrict__ gnorm_out = nullptr,
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, 
     // pool's matrices sit on different SM sub-partitions); later chunks are
     // claimed through the shared counter.
     __shared__ int pool_next;
-    if (threadIdx.x == 0) pool_next = 32 * kFwdWarps;
+    if (threadIdx.x == 0) pool_next = 32 * kWarps;
     __syncthreads();
     int cnt = 0;  // matrices this warp has claimed (positions [0, cnt) of its sequence)
     src.advance(begin);
@@ -191,11 +196,11 @@ __global__ void __launch_bounds__(kNewtonBlock, 1) birkhoff_fwd_kernel(Src src, 
     extern __shared__ float4 ring_dyn[];
     float4 (*ring_all)[kRing * kSlot + 1] = reinterpret_cast<float4 (*)[kRing * kSlot + 1]>(ring_dyn);
     // the block offsets of the two chunks in the warp's ring
-    __shared__ int chunk_all[kNewtonBlock / 32][2];
+    __shared__ int chunk_all[kWarps][2];
     int* chunk = chunk_all[threadIdx.x >> 5];
     // The line-search steps gamma_k as a per-warp table: one shared load per
     // step instead of a chain of compares and selects.
-    __shared__ float gtab_all[kNewtonBlock / 32][8];
+    __shared__ float gtab_all[kWarps][8];
     float* gtab = gtab_all[threadIdx.x >> 5];
     if (lane < 8) gtab[lane] = line_step(lane);
     __syncwarp();
@@ -711,11 +716,11 @@ __global__ void __launch_bounds__(kHResBlock) birkhoff_hres_bwd_kernel(
 // queried once per device and instantiation (so later launches make no extra
 // runtime calls, which also keeps them legal inside stream capture).
 constexpr int kMaxDevices = 64;
-// Dynamic shared memory of a forward block: each warp's ring (64 slots of
-// five 16-byte entries) and its output pointer.
-constexpr int kFwdRingBytes = kFwdWarps * (kRing * 5 + 1) * 16;
+// Dynamic shared memory of a forward block of kWarps warps: each warp's ring
+// (64 slots of five 16-byte entries) and its output pointer.
+constexpr int fwd_ring_bytes(int warps) { return warps * (kRing * 5 + 1) * 16; }
 
-template <auto kKernel>
+template <auto kKernel, int kWarps>
 static int64_t forward_block_slots()
 {
     static std::atomic<int64_t> cache[kMaxDevices];  // per instantiation; 0 = not queried yet
@@ -727,9 +732,11 @@ static int64_t forward_block_slots()
     }
     int sms = 0, blocks = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    if (cudaFuncSetAttribute(kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdRingBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kKernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd_ring_bytes(kWarps)) !=
+        cudaSuccess)
         return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, kNewtonBlock, kFwdRingBytes) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, 32 * kWarps, fwd_ring_bytes(kWarps)) !=
+            cudaSuccess ||
         blocks < 1)
         return 0;
     const int64_t slots = static_cast<int64_t>(sms) * blocks;  // resident blocks
@@ -737,12 +744,14 @@ static int64_t forward_block_slots()
     return slots;
 }
 
-template <class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
-static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters = nullptr,
-                          float* gnorm = nullptr, float* beta = nullptr, unsigned long long* counts = nullptr)
+template <class Src, class Elem, bool kVec, bool kStats, bool kDuals, int kWarps>
+static int launch_forward_warps(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters,
+                                float* gnorm, float* beta, unsigned long long* counts)
 {
-    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats, kDuals>;
-    const int64_t slots = forward_block_slots<kernel>();
+    constexpr auto kernel = birkhoff_fwd_kernel<RefRounding, Src, Elem, kVec, kStats, kDuals, kWarps>;
+    constexpr int kBlock = 32 * kWarps;
+    constexpr int kSmem = fwd_ring_bytes(kWarps);
+    const int64_t slots = forward_block_slots<kernel, kWarps>();
     if (slots <= 0) {
         const cudaError_t e = cudaGetLastError();
         return static_cast<int>(e != cudaSuccess ? e : cudaErrorUnknown);
@@ -752,19 +761,30 @@ static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t s
     const int64_t blocks = max(min(ceil_div(N, 32), slots), ceil_div(N, int64_t{1} << 30));
     const int64_t per_block = ceil_div(N, blocks);
     const int64_t grid = ceil_div(N, per_block);
-    kernel<<<grid, kNewtonBlock, kFwdRingBytes, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters,
-                                                          gnorm, beta, counts);
+    kernel<<<grid, kBlock, kSmem, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters, gnorm, beta,
+                                            counts);
     cudaError_t e = cudaGetLastError();
     if (e == cudaErrorInvalidValue &&
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdRingBytes) == cudaSuccess) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) == cudaSuccess) {
         // The shared-memory attribute belongs to the CUDA context: after a
         // device reset the cached launch shape is still right but the
         // attribute is gone, so set it again and launch once more.
-        kernel<<<grid, kNewtonBlock, kFwdRingBytes, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters,
-                                                              gnorm, beta, counts);
+        kernel<<<grid, kBlock, kSmem, stream>>>(src, static_cast<Elem*>(T), tol, N, per_block, iters, gnorm, beta,
+                                                counts);
         e = cudaGetLastError();
     }
     return static_cast<int>(e);
+}
+
+template <class Src, class Elem, bool kVec, bool kStats = false, bool kDuals = false>
+static int launch_forward(Src src, void* T, float tol, int64_t N, cudaStream_t stream, int32_t* iters = nullptr,
+                          float* gnorm = nullptr, float* beta = nullptr, unsigned long long* counts = nullptr)
+{
+    if (N > kFwdWideN)
+        return launch_forward_warps<Src, Elem, kVec, kStats, kDuals, kFwdWarpsThroughput>(src, T, tol, N, stream,
+                                                                                          iters, gnorm, beta, counts);
+    return launch_forward_warps<Src, Elem, kVec, kStats, kDuals, kFwdWarpsLatency>(src, T, tol, N, stream, iters,
+                                                                                   gnorm, beta, counts);
 }
 
 
