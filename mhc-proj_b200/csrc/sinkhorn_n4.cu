@@ -18,10 +18,6 @@ namespace mhcp {
 
 constexpr float kSkEps = 1e-8f;  // src/sinkhorn_knopp_n4.cu:10,18
 constexpr int kSkBlock = 128;
-// The backward replays the forward with the hardware reciprocal (sk_inv_approx):
-// its gradient must be that of the forward within tolerance, not bitwise, and
-// the correctly rounded reciprocal is most of the replay's cost.
-constexpr bool kSkBwdApprox = true;
 
 
 // exp of every entry (the fused kernels' input is the logits R).
@@ -92,88 +88,48 @@ __global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restri
     in.template load<kVec>(idx, x0);
     Pairs x = to_pairs(x0);
 #pragma unroll 1
-    for (int it = 0; it < iters; ++it) sk_iteration<kApprox>(x, kSkEps, nullptr, nullptr, nullptr);
+    for (int it = 0; it < iters; ++it) sk_iteration<kApprox>(x, kSkEps);
     store_mat<kVec>(T, idx, from_pairs(x));
 }
 
-// The vector-Jacobian product of kIters Sinkhorn-Knopp iterations at x, in
-// two halves so that the caller loads the incoming gradient only after the
-// first: sk_checkpoint runs the forward and keeps each segment's start in
-// shared memory, [segment][element][thread] so that a warp's accesses fall
-// in distinct banks; sk_reverse replays each segment in registers and
-// reverses it into dy.
+// History rows of a kIters backward (at least one).
 template <int kIters>
-__device__ __forceinline__ void sk_checkpoint(Pairs x, float2 (*ckpt)[8][kSkBlock], int tid)
-{
-    constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-    // Segments are not unrolled: the 20-iteration body unrolled five times
-    // overflowed the instruction cache (instruction-fetch stalls first) and
-    // needed 167 registers instead of 122.
-#pragma unroll 1
-    for (int s = 0; s < kNumSeg; ++s) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) ckpt[s][q][tid] = x.p[q];
-        if (s + 1 < kNumSeg) {
-#pragma unroll
-            for (int k = 0; k < kSkSeg; ++k) sk_iteration<kSkBwdApprox>(x, kSkEps, nullptr, nullptr, nullptr);
-        }
-    }
-}
+constexpr int kSkHist = kIters > 0 ? kIters : 1;
 
-template <int kIters>
-__device__ __forceinline__ void sk_reverse(Pairs& dy, float2 (*ckpt)[8][kSkBlock], int tid)
-{
-    constexpr int kNumSeg = (kIters + kSkSeg - 1) / kSkSeg;
-#pragma unroll 1
-    for (int s = kNumSeg - 1; s >= 0; --s) {
-        const int len = (s == kNumSeg - 1) ? (kIters - s * kSkSeg) : kSkSeg;
-        Pairs x, xr[kSkSeg];
-        float ri[kSkSeg][4], ci[kSkSeg][4];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) x.p[q] = ckpt[s][q][tid];
-#pragma unroll
-        for (int k = 0; k < kSkSeg; ++k)
-            if (k < len) sk_iteration<kSkBwdApprox>(x, kSkEps, &xr[k], ri[k], ci[k]);
-#pragma unroll
-        for (int k = kSkSeg - 1; k >= 0; --k)
-            if (k < len) sk_iteration_vjp(dy, xr[k], ri[k], ci[k]);
-    }
-}
-
-// Checkpoint segments of a kIters backward (at least one array row).
-template <int kIters>
-constexpr int kSkSegments = (kIters + kSkSeg - 1) / kSkSeg > 0 ? (kIters + kSkSeg - 1) / kSkSeg : 1;
-
-// Backward with a compile-time iteration count: D = dL/dM, or with
-// kLogits (ExpInput) the gradient with respect to R, dL/dM * exp(R).
+// Backward with a compile-time iteration count, in potential form
+// (sinkhorn_n4.cuh): D = dL/dM, or with kLogits (ExpInput) the gradient with
+// respect to R, dL/dM * exp(R).  v_1 .. v_kIters in shared memory,
+// [iteration][thread] so that a warp's 16-byte accesses are conflict-free.
 template <int kIters, bool kVec, bool kLogits>
 __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restrict__ G,
                                                           const float* __restrict__ M,
                                                           float* __restrict__ D, int64_t N)
 {
-    __shared__ float2 ckpt[kSkSegments<kIters>][8][kSkBlock];
+    __shared__ float4 vh[kSkHist<kIters>][kSkBlock];
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
-    {
-        Mat4 x0;
-        if constexpr (kLogits)
-            ExpInput{M}.load<kVec>(idx, x0);
-        else
-            MInput{M}.load<kVec>(idx, x0);
-        sk_checkpoint<kIters>(to_pairs(x0), ckpt, threadIdx.x);
+    Mat4 x0, g0;
+    if constexpr (kLogits)
+        ExpInput{M}.load<kVec>(idx, x0);
+    else
+        MInput{M}.load<kVec>(idx, x0);
+    const Pairs m = to_pairs(x0);
+    Pairs d;
+    if constexpr (kIters > 0) {
+        bool mr[4];
+        float u[4], v[4];
+        pot_forward<kIters, kSkBlock>(m, kSkEps, vh, threadIdx.x, mr, u, v);
+        load_mat<kVec>(G, idx, g0);
+        pot_reverse<kIters, kSkBlock>(m, to_pairs(g0), vh, threadIdx.x, mr, u, v, d);
+    } else {
+        load_mat<kVec>(G, idx, g0);
+        d = to_pairs(g0);
     }
-    Mat4 g0;
-    load_mat<kVec>(G, idx, g0);
-    Pairs dy = to_pairs(g0);
-    sk_reverse<kIters>(dy, ckpt, threadIdx.x);
     if constexpr (kLogits) {
-        Mat4 m;
-        ExpInput{M}.load<kVec>(idx, m);
-        const Pairs mp = to_pairs(m);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) dy.p[q] = __fmul2_rn(dy.p[q], mp.p[q]);
+        for (int q = 0; q < 8; ++q) d.p[q] = __fmul2_rn(d.p[q], m.p[q]);
     }
-    store_mat<kVec>(D, idx, from_pairs(dy));
+    store_mat<kVec>(D, idx, from_pairs(d));
 }
 
 // Backward of the producer fused with Sinkhorn-Knopp: dM as above, dR = dM *
@@ -186,25 +142,26 @@ __global__ void __launch_bounds__(kSkBlock) sk_hres_bwd_kernel(const float* __re
                                                                float* __restrict__ drms,
                                                                float* __restrict__ partials, int64_t N)
 {
-    __shared__ float2 ckpt[kSkSegments<kIters>][8][kSkBlock];
+    __shared__ float4 vh[kSkHist<kIters>][kSkBlock];
     float acc[kHResPartials];
 #pragma unroll
     for (int q = 0; q < kHResPartials; ++q) acc[q] = 0.0f;
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx < N) {
-        {
-            Mat4 x0;
-            in.load<kVec>(idx, x0);
-            sk_checkpoint<kIters>(to_pairs(x0), ckpt, threadIdx.x);
-        }
-        Mat4 g0;
-        load_mat<kVec>(G, idx, g0);
-        Pairs dy = to_pairs(g0);
-        sk_reverse<kIters>(dy, ckpt, threadIdx.x);
-        Mat4 hx, m, dR, dx;
+        Mat4 hx, m, g0, dR, dx;
         const float rinv = in.load_h<kVec>(idx, hx);
         in.activate(hx, rinv, m);
-        const Mat4 dM = from_pairs(dy);
+        const Pairs mp = to_pairs(m);
+        load_mat<kVec>(G, idx, g0);
+        Mat4 dM = g0;
+        if constexpr (kIters > 0) {
+            bool mr[4];
+            float u[4], v[4];
+            Pairs d;
+            pot_forward<kIters, kSkBlock>(mp, kSkEps, vh, threadIdx.x, mr, u, v);
+            pot_reverse<kIters, kSkBlock>(mp, to_pairs(g0), vh, threadIdx.x, mr, u, v, d);
+            dM = from_pairs(d);
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) dR.m[e] = __fmul_rn(dM.m[e], m.m[e]);
         drms[idx] = hres_chain(dR, hx, __ldg(in.alpha), rinv, dx, acc);

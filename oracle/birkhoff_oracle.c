@@ -17,9 +17,11 @@
  *       (eps passed by src/sinkhorn_knopp_n4.cu:10)
  *   - the Sinkhorn-Knopp n4 backward, two versions (sk_backward_one):
  *       * exact: the exact vector-Jacobian product of the forward (what
- *         PyTorch autograd of the same forward gives), with its sums formed
- *         as the left-to-right FMA chains of this repository's kernel and
- *         each step as the kernel's fused multiply-add;
+ *         PyTorch autograd of the same forward gives), differentiated step by
+ *         step through the row/column form (sums as left-to-right FMA
+ *         chains, each update as one fused multiply-add) -- an independent
+ *         statement of the gradient that the GPU kernel forms from the
+ *         forward's potentials;
  *       * reference row step: the reference kernel's reverse loop
  *         src/sinkhorn_knopp.cuh:1146-1202 including its row step
  *         (d - r*rinv)*rinv at :1182-1201, which differs from the exact VJP
@@ -343,7 +345,7 @@ static void sk_backward_one(const float G[16], const float M[16], float D[16],
         /* column step y = x * cinv: dx = (dy - cinv_j sum_k dy_kj x_kj) cinv_j */
         for (int j = 0; j < 4; j++) {
             float cs;
-            if (exact) { /* the sum as this repository's kernel forms it: a left-to-right FMA chain */
+            if (exact) { /* a left-to-right FMA chain */
                 cs = dx[j] * xr[j];
                 cs = fmaf(dx[4 + j], xr[4 + j], cs);
                 cs = fmaf(dx[8 + j], xr[8 + j], cs);
@@ -351,7 +353,7 @@ static void sk_backward_one(const float G[16], const float M[16], float D[16],
             } else {     /* as the reference's build contracts ((a+b)+c)+d of products */
                 cs = fmaf(dx[12 + j], xr[12 + j], fmaf(dx[8 + j], xr[8 + j], fmaf(dx[j], xr[j], dx[4 + j] * xr[4 + j])));
             }
-            if (exact) { /* fma(dy, cinv, -((cs cinv) cinv)), as the kernel forms it */
+            if (exact) { /* fma(dy, cinv, -((cs cinv) cinv)) */
                 const float t = (cs * ci[it][j]) * ci[it][j];
                 for (int i = 0; i < 4; i++) dx[4 * i + j] = fmaf(dx[4 * i + j], ci[it][j], -t);
             } else {
@@ -372,7 +374,7 @@ static void sk_backward_one(const float G[16], const float M[16], float D[16],
             } else {
                 rs = fmaf(d4[3], x4[3], fmaf(d4[2], x4[2], fmaf(d4[0], x4[0], d4[1] * x4[1])));
             }
-            if (exact) { /* fma(dx, rinv, -(rs rinv)), as the kernel forms it */
+            if (exact) { /* fma(dx, rinv, -(rs rinv)) */
                 const float t = rs * ri[it][i];
                 for (int j = 0; j < 4; j++) dx[4 * i + j] = fmaf(dx[4 * i + j], ri[it][i], -t);
             } else {

@@ -180,11 +180,12 @@ def test_sinkhorn_pair_matches_vanilla_autograd():
 
 @pytest.mark.parametrize("iters", [1, 2, 3, 4, 5, 9, 16, 19, 20])
 def test_sinkhorn_backward_every_iteration_count(iters):
-    """The exact VJP for every iteration count: against the oracle's (which
-    replays the forward with correctly rounded reciprocals) within 2e-6,
-    relative where |dM| > 1 -- the kernel's replay uses the hardware
-    reciprocal (one ulp), and dM = dR / M grows where M is small -- and dR
-    within 1e-5 of vanilla autograd."""
+    """The exact VJP for every iteration count: against the oracle's (the
+    row/column form differentiated step by step, with correctly rounded
+    reciprocals) within 2e-6, relative where |dM| > 1 -- the kernel forms the
+    gradient from the forward's potentials with the hardware reciprocal (one
+    ulp), and dM = dR / M grows where M is small -- and dR within 1e-5 of
+    vanilla autograd."""
     n = 4096
     M = torch.exp(make_logits("normal", n, seed=iters))
     G = make_logits("normal", n, seed=iters + 50)
