@@ -197,6 +197,43 @@ def test_sinkhorn_backward_every_iteration_count(iters):
     assert (D * M - dRv).abs().max().item() < TOL
 
 
+@pytest.mark.parametrize("iters", [1, 2, 5, 20])
+def test_sinkhorn_backward_masked_rows_and_columns(iters):
+    """Rows and columns whose sums fall to eps or below get a zero factor
+    (sinkhorn_knopp.cuh:851-906).  The kernel takes its masks from the first
+    iteration only (no later row or column can fall that low); the oracle
+    tests every iteration.  Matrices with a row of logits -40 (row sum below
+    eps), a column of -40 (its sum below eps after the row step), both, two
+    such rows, and rows or columns just above the threshold: the same zero
+    pattern, dR = dM * M within 2e-6, and dM within 2e-6 relative wherever
+    M > 1e-6 (below that dM = dR / M carries both sides' rounding, amplified)."""
+    n = 4096
+    g = torch.Generator().manual_seed(70 + iters)
+    R = torch.randn(n, 4, 4, generator=g)
+    for m in range(n):
+        i, j, c = m % 4, (m // 4) % 4, m % 8
+        if c in (1, 3):
+            R[m, i, :] = -40.0
+        if c in (2, 3):
+            R[m, :, j] = -40.0
+        if c == 4:
+            R[m, i, :] = -19.5  # row sum 1.3e-8: just above eps
+        if c == 5:
+            R[m, :, j] = -21.0
+        if c == 6:
+            R[m, i, :] = -40.0
+            R[m, (i + 1) % 4, :] = -40.0
+    G = torch.randn(n, 4, 4, generator=g)
+    M = torch.exp(R)
+    D = capi.sinkhorn_knopp_n4_backward_tensor(G.cuda(), M.cuda(), iters).cpu().numpy()
+    Mn = M.numpy()
+    Do = oracle.sinkhorn_knopp_n4_backward(G.numpy(), Mn, iters, 1e-8, exact=True)
+    assert np.array_equal(D == 0, Do == 0)
+    assert (np.abs(D * Mn - Do * Mn) <= 2e-6).all()
+    big = Mn > 1e-6
+    assert (np.abs(D - Do)[big] <= 2e-6 * np.maximum(1.0, np.abs(Do[big]))).all()
+
+
 def test_sinkhorn_backward_zero_iterations_is_identity():
     M = torch.exp(make_logits("normal", 1000, seed=1))
     G = make_logits("normal", 1000, seed=2)
