@@ -7,7 +7,10 @@ on the same device and the same inputs, CUDA-event timing after warm-up:
     from a CUDA graph (host launch overhead excluded), each call on a fresh
     input from a pool of 8: within 5% of the reference (the
     two-lanes-per-matrix kernels below 2^13 measured from 4% faster to 1%
-    slower than it) and not slower at 2^13 and 2^14.
+    slower than it) and not slower at 2^13 and 2^14;
+  - the fused exp + Sinkhorn-Knopp pair at N = 2^22 at least 2x faster per
+    forward + backward than the reference's MHCSinkhornN4 composition on its
+    own kernels.
 The measured times are printed."""
 import pytest
 import torch
@@ -110,3 +113,33 @@ def test_small_batches_against_reference_kernels(kind):
             a, b = _graph_us_per_call(ours), _graph_us_per_call(theirs)
             print(f"\n[{kind} N=2^{lg} {'fwd+bwd' if backward else 'fwd'}] this {a:.1f} us, reference {b:.1f} us")
             assert a <= (1.0 if lg >= 13 else 1.05) * b, (kind, lg, backward, a, b)
+
+
+def test_sinkhorn_pair_faster_than_reference_composition():
+    """The fused exp + Sinkhorn-Knopp pair (20 iterations, N = 2^22) against
+    the reference's MHCSinkhornN4 composition on its own kernels (module.py:
+    torch.exp, its sinkhorn_knopp_n4, its backward, the product with exp(R)):
+    at least 2x faster per forward + backward step."""
+    if not oracle.RefCuda.available():
+        pytest.skip("reference kernels not built")
+    ref = oracle.RefCuda()
+    n = 1 << 22
+    R = make_logits("normal", n, seed=0)
+    G = make_logits("normal", n, seed=1)
+    T = torch.empty_like(R)
+    D = torch.empty_like(R)
+    s = torch.cuda.current_stream().cuda_stream
+
+    def ours():
+        capi.sinkhorn_knopp_n4_logits(R.data_ptr(), T.data_ptr(), n, 20, s)
+        capi.sinkhorn_knopp_n4_logits_backward(G.data_ptr(), R.data_ptr(), D.data_ptr(), n, 20, s)
+
+    def theirs():
+        M = torch.exp(R)
+        ref.sinkhorn_knopp_n4(M.data_ptr(), T.data_ptr(), n, 20, s)
+        ref.sinkhorn_knopp_n4_backward(G.data_ptr(), M.data_ptr(), D.data_ptr(), n, 20, s)
+        D.mul_(M)
+
+    a, b = _ms(ours), _ms(theirs)
+    print(f"\n[SK20 N=2^22 fwd+bwd] this {a:.3f} ms, reference composition {b:.3f} ms ({b / a:.2f}x)")
+    assert b / a > 2.0
