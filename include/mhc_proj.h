@@ -167,13 +167,18 @@ MHC_API int mhc_sinkhorn_knopp_n4_backward(const float* d_G, const float* d_M, f
 MHC_API int mhc_sinkhorn_knopp_n4_logits(const float* d_R, float* d_T, int64_t N, int num_iters,
                                          cudaStream_t stream);
 
-/* Flags of mhc_sinkhorn_knopp_n4_logits_ex. */
+/* Flags of mhc_sinkhorn_knopp_n4_logits_ex and of the strided entry points
+ * below. */
 enum {
     /* The normalisation factors from the hardware reciprocal (at most one
      * ulp from 1/s) instead of the correctly rounded one: not the reference
      * kernel's bits, but within 1e-6 of them and of the vanilla PyTorch
      * Sinkhorn-Knopp on N(0,1) logits, and about 20% faster. */
-    MHC_SK_HW_RECIPROCAL = 1
+    MHC_SK_HW_RECIPROCAL = 1,
+    /* (strided entry points) The input is the logits R: M = exp(R), the
+     * accurate expf rounded to R's storage type, as torch.exp in that type
+     * computes it. */
+    MHC_SK_LOGITS = 2
 };
 
 /* mhc_sinkhorn_knopp_n4_logits with `flags` (0 or MHC_SK_HW_RECIPROCAL; any
@@ -189,6 +194,31 @@ MHC_API int mhc_sinkhorn_knopp_n4_logits_ex(const float* d_R, float* d_T, int64_
  * MHC_ERR_ITERS. */
 MHC_API int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const float* d_R, float* d_D,
                                                   int64_t N, int num_iters, cudaStream_t stream);
+
+/* mhc_sinkhorn_knopp_n4 (or, with MHC_SK_LOGITS, the fused-exponential form)
+ * on a strided batch of any storage type: matrix k of X starts at element
+ * k * x_stride (its 16 entries row-major and contiguous); T is written
+ * contiguous in the same type.  The results are the reference's on such a
+ * tensor: its wrapper converts X to contiguous fp32 and T back
+ * (solvers_torch.cpp:190,196,211), its module computes torch.exp in X's type
+ * (mhc_proj/module.py:50); bf16 and fp16 widen exactly and T is rounded to
+ * nearest even.  flags: MHC_SK_LOGITS, MHC_SK_HW_RECIPROCAL.  No reference
+ * counterpart. */
+MHC_API int mhc_sinkhorn_knopp_n4_strided(const void* d_X, int64_t x_stride, void* d_T, int dtype, int64_t N,
+                                          int num_iters, int flags, cudaStream_t stream);
+
+/* The backward of mhc_sinkhorn_knopp_n4_strided: G (g_dtype, stride g_stride
+ * elements) and X (x_dtype, stride x_stride: M, or with MHC_SK_LOGITS the
+ * logits R); D is written contiguous in G's type.  Without MHC_SK_LOGITS, D is
+ * dL/dM rounded to G's type (the reference wrapper's result,
+ * solvers_torch.cpp:258-266,282); with it, that rounded dL/dM times M rounded to
+ * G's type again -- the reference module's D * expon (mhc_proj/module.py:70)
+ * when G and R have the same type.  flags: MHC_SK_LOGITS only.  num_iters >
+ * MHC_SK_BACKWARD_MAX_ITERS returns MHC_ERR_ITERS.  No reference
+ * counterpart. */
+MHC_API int mhc_sinkhorn_knopp_n4_backward_strided(const void* d_G, int64_t g_stride, int g_dtype, const void* d_X,
+                                                   int64_t x_stride, int x_dtype, void* d_D, int64_t N,
+                                                   int num_iters, int flags, cudaStream_t stream);
 
 /* The projection fused with its producer, the H_res pre-activation of an
  * mHC layer: R[k] = alpha * h[k] / rms[k] + b, formed in the kernel's load

@@ -77,10 +77,31 @@ struct HResInput {
     }
 };
 
+// A batch of any storage type at any batch stride: matrix idx of X starts at
+// element idx * stride (its 16 entries row-major and contiguous).  kExp: X is
+// the logits and M = exp(X) with the accurate expf rounded to Elem -- what
+// torch.exp computes in that type (the reference's MHCSinkhornN4Function,
+// mhc_proj/module.py:50) -- else M = X.  bf16 and fp16 widen exactly.
+template <class Elem, bool kExp>
+struct TypedInput {
+    const Elem* X;
+    int64_t stride;
+    template <bool kVec>
+    __device__ __forceinline__ void load(int64_t idx, Mat4& x) const
+    {
+        load_elems<Elem, kVec>(X, idx * stride, x);
+        if constexpr (kExp) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) x.m[e] = to_f32(from_f32<Elem>(expf(x.m[e])));
+        }
+    }
+};
+
 // kApprox: the factors from the hardware reciprocal (sk_inv_approx) instead
-// of the correctly rounded one.
-template <bool kVec, class In, bool kApprox = false>
-__global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restrict__ T, int64_t N, int iters)
+// of the correctly rounded one.  TOut: the storage type of T (contiguous;
+// round-to-nearest-even from fp32, as torch's .to()).
+template <bool kVec, class In, bool kApprox = false, class TOut = float>
+__global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, TOut* __restrict__ T, int64_t N, int iters)
 {
     const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (idx >= N) return;
@@ -89,7 +110,7 @@ __global__ void __launch_bounds__(kSkBlock) sk_fwd_kernel(In in, float* __restri
     Pairs x = to_pairs(x0);
 #pragma unroll 1
     for (int it = 0; it < iters; ++it) sk_iteration<kApprox>(x, kSkEps);
-    store_mat<kVec>(T, idx, from_pairs(x));
+    store_elems<TOut, kVec>(T, idx * 16, from_pairs(x));
 }
 
 // History rows of a kIters backward (at least one).
@@ -118,9 +139,9 @@ __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restric
     if constexpr (kIters > 0) {
         bool mr[4];
         float u[4], v[4];
-        pot_forward<kIters, kSkBlock>(m, kSkEps, vh, threadIdx.x, mr, u, v);
+        pot_forward<kSkBlock>(m, kSkEps, vh, threadIdx.x, kIters, mr, u, v);
         load_mat<kVec>(G, idx, g0);
-        pot_reverse<kIters, kSkBlock>(m, to_pairs(g0), vh, threadIdx.x, mr, u, v, d);
+        pot_reverse<kSkBlock>(m, to_pairs(g0), vh, threadIdx.x, kIters, mr, u, v, d);
     } else {
         load_mat<kVec>(G, idx, g0);
         d = to_pairs(g0);
@@ -130,6 +151,44 @@ __global__ void __launch_bounds__(kSkBlock) sk_bwd_kernel(const float* __restric
         for (int q = 0; q < 8; ++q) d.p[q] = __fmul2_rn(d.p[q], m.p[q]);
     }
     store_mat<kVec>(D, idx, from_pairs(d));
+}
+
+// The backward on batches of any storage types at any batch strides, the
+// iteration count at run time (1..kSkMaxIters; 0 gives D = G): G of type GE,
+// X of type XE (M, or with kLogits the logits R and M = exp(R) rounded to XE
+// as TypedInput forms it), D contiguous in GE.  The results are those of the
+// reference's wrappers and module on such tensors: D = dL/dM rounded to GE
+// (solvers_torch.cpp's D.to(G.dtype)), and with kLogits that rounded D times
+// M rounded to GE again (mhc_proj/module.py:70, D * expon in the tensors'
+// type).
+template <bool kVec, class GE, class XE, bool kLogits>
+__global__ void __launch_bounds__(kSkBlock) sk_bwd_typed_kernel(const GE* __restrict__ G, int64_t g_stride,
+                                                                TypedInput<XE, kLogits> in, GE* __restrict__ D,
+                                                                int64_t N, int iters)
+{
+    __shared__ float4 vh[kSkMaxIters][kSkBlock];
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= N) return;
+    Mat4 x0, g0;
+    in.template load<kVec>(idx, x0);
+    const Pairs m = to_pairs(x0);
+    Mat4 out;
+    if (iters > 0) {
+        bool mr[4];
+        float u[4], v[4];
+        Pairs d;
+        pot_forward<kSkBlock>(m, kSkEps, vh, threadIdx.x, iters, mr, u, v);
+        load_elems<GE, kVec>(G, idx * g_stride, g0);
+        pot_reverse<kSkBlock>(m, to_pairs(g0), vh, threadIdx.x, iters, mr, u, v, d);
+        out = from_pairs(d);
+    } else {
+        load_elems<GE, kVec>(G, idx * g_stride, out);
+    }
+    if constexpr (kLogits) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) out.m[e] = __fmul_rn(to_f32(from_f32<GE>(out.m[e])), x0.m[e]);
+    }
+    store_elems<GE, kVec>(D, idx * 16, out);
 }
 
 // Backward of the producer fused with Sinkhorn-Knopp: dM as above, dR = dM *
@@ -158,8 +217,8 @@ __global__ void __launch_bounds__(kSkBlock) sk_hres_bwd_kernel(const float* __re
             bool mr[4];
             float u[4], v[4];
             Pairs d;
-            pot_forward<kIters, kSkBlock>(mp, kSkEps, vh, threadIdx.x, mr, u, v);
-            pot_reverse<kIters, kSkBlock>(mp, to_pairs(g0), vh, threadIdx.x, mr, u, v, d);
+            pot_forward<kSkBlock>(mp, kSkEps, vh, threadIdx.x, kIters, mr, u, v);
+            pot_reverse<kSkBlock>(mp, to_pairs(g0), vh, threadIdx.x, kIters, mr, u, v, d);
             dM = from_pairs(d);
         }
 #pragma unroll
@@ -235,6 +294,73 @@ static void dispatch_sk_hres_bwd(int iters, bool vec, const float* G, const HRes
      ...);
 }
 
+static bool sk_valid_dtype(int dt) { return dt == MHC_DTYPE_F32 || dt == MHC_DTYPE_BF16 || dt == MHC_DTYPE_F16; }
+
+template <class Elem, bool kLogits, bool kApprox>
+static void sk_forward_typed(const void* X, int64_t x_stride, void* T, int64_t N, int iters, cudaStream_t stream)
+{
+    using In = TypedInput<Elem, kLogits>;
+    const In in{static_cast<const Elem*>(X), x_stride};
+    Elem* t = static_cast<Elem*>(T);
+    const int64_t grid = ceil_div(N, kSkBlock);
+    if (aligned16(X, x_stride, sizeof(Elem)) && aligned16(T))
+        sk_fwd_kernel<true, In, kApprox, Elem><<<grid, kSkBlock, 0, stream>>>(in, t, N, iters);
+    else
+        sk_fwd_kernel<false, In, kApprox, Elem><<<grid, kSkBlock, 0, stream>>>(in, t, N, iters);
+}
+
+template <class Elem>
+static void sk_forward_typed(const void* X, int64_t x_stride, void* T, int64_t N, int iters, int flags,
+                             cudaStream_t stream)
+{
+    const bool logits = flags & MHC_SK_LOGITS, approx = flags & MHC_SK_HW_RECIPROCAL;
+    if (logits)
+        approx ? sk_forward_typed<Elem, true, true>(X, x_stride, T, N, iters, stream)
+               : sk_forward_typed<Elem, true, false>(X, x_stride, T, N, iters, stream);
+    else
+        approx ? sk_forward_typed<Elem, false, true>(X, x_stride, T, N, iters, stream)
+               : sk_forward_typed<Elem, false, false>(X, x_stride, T, N, iters, stream);
+}
+
+template <class GE, class XE, bool kLogits>
+static void sk_backward_typed(const void* G, int64_t g_stride, const void* X, int64_t x_stride, void* D, int64_t N,
+                              int iters, cudaStream_t stream)
+{
+    const TypedInput<XE, kLogits> in{static_cast<const XE*>(X), x_stride};
+    const GE* g = static_cast<const GE*>(G);
+    GE* d = static_cast<GE*>(D);
+    const int64_t grid = ceil_div(N, kSkBlock);
+    if (aligned16(G, g_stride, sizeof(GE)) && aligned16(X, x_stride, sizeof(XE)) && aligned16(D))
+        sk_bwd_typed_kernel<true, GE, XE, kLogits><<<grid, kSkBlock, 0, stream>>>(g, g_stride, in, d, N, iters);
+    else
+        sk_bwd_typed_kernel<false, GE, XE, kLogits><<<grid, kSkBlock, 0, stream>>>(g, g_stride, in, d, N, iters);
+}
+
+template <class GE, bool kLogits>
+static void sk_backward_typed(const void* G, int64_t g_stride, const void* X, int64_t x_stride, int x_dtype,
+                              void* D, int64_t N, int iters, cudaStream_t stream)
+{
+    switch (x_dtype) {
+        case MHC_DTYPE_BF16:
+            return sk_backward_typed<GE, __nv_bfloat16, kLogits>(G, g_stride, X, x_stride, D, N, iters, stream);
+        case MHC_DTYPE_F16: return sk_backward_typed<GE, __half, kLogits>(G, g_stride, X, x_stride, D, N, iters, stream);
+        default: return sk_backward_typed<GE, float, kLogits>(G, g_stride, X, x_stride, D, N, iters, stream);
+    }
+}
+
+template <bool kLogits>
+static void sk_backward_typed(const void* G, int64_t g_stride, int g_dtype, const void* X, int64_t x_stride,
+                              int x_dtype, void* D, int64_t N, int iters, cudaStream_t stream)
+{
+    switch (g_dtype) {
+        case MHC_DTYPE_BF16:
+            return sk_backward_typed<__nv_bfloat16, kLogits>(G, g_stride, X, x_stride, x_dtype, D, N, iters, stream);
+        case MHC_DTYPE_F16:
+            return sk_backward_typed<__half, kLogits>(G, g_stride, X, x_stride, x_dtype, D, N, iters, stream);
+        default: return sk_backward_typed<float, kLogits>(G, g_stride, X, x_stride, x_dtype, D, N, iters, stream);
+    }
+}
+
 }  // namespace mhcp
 
 using namespace mhcp;
@@ -268,6 +394,55 @@ extern "C" int mhc_sinkhorn_knopp_n4_logits_backward(const float* d_G, const flo
                                                      int num_iters, cudaStream_t stream)
 {
     return sk_backward<true>(d_G, d_R, d_D, N, num_iters, stream);
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_strided(const void* d_X, int64_t x_stride, void* d_T, int dtype, int64_t N,
+                                             int num_iters, int flags, cudaStream_t stream)
+{
+    if (N < 0 || x_stride < 0 || !sk_valid_dtype(dtype) || (flags & ~(MHC_SK_HW_RECIPROCAL | MHC_SK_LOGITS)) ||
+        (N > 0 && (!d_X || !d_T)))
+        return MHC_ERR_INVALID_VALUE;
+    if (N == 0) return MHC_OK;
+    const int iters = num_iters > 0 ? num_iters : 0;
+    switch (dtype) {
+        case MHC_DTYPE_BF16: sk_forward_typed<__nv_bfloat16>(d_X, x_stride, d_T, N, iters, flags, stream); break;
+        case MHC_DTYPE_F16: sk_forward_typed<__half>(d_X, x_stride, d_T, N, iters, flags, stream); break;
+        default:
+            if (x_stride == 16)  // the contiguous fp32 kernels
+                return (flags & MHC_SK_LOGITS)
+                           ? mhc_sinkhorn_knopp_n4_logits_ex(static_cast<const float*>(d_X), static_cast<float*>(d_T),
+                                                             N, num_iters, flags & MHC_SK_HW_RECIPROCAL, stream)
+                           : ((flags & MHC_SK_HW_RECIPROCAL)
+                                  ? sk_forward<false, true>(static_cast<const float*>(d_X), static_cast<float*>(d_T),
+                                                            N, num_iters, stream)
+                                  : sk_forward<false>(static_cast<const float*>(d_X), static_cast<float*>(d_T), N,
+                                                      num_iters, stream));
+            sk_forward_typed<float>(d_X, x_stride, d_T, N, iters, flags, stream);
+    }
+    return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int mhc_sinkhorn_knopp_n4_backward_strided(const void* d_G, int64_t g_stride, int g_dtype, const void* d_X,
+                                                      int64_t x_stride, int x_dtype, void* d_D, int64_t N,
+                                                      int num_iters, int flags, cudaStream_t stream)
+{
+    if (N < 0 || g_stride < 0 || x_stride < 0 || !sk_valid_dtype(g_dtype) || !sk_valid_dtype(x_dtype) ||
+        (flags & ~MHC_SK_LOGITS) || (N > 0 && (!d_G || !d_X || !d_D)))
+        return MHC_ERR_INVALID_VALUE;
+    if (num_iters > MHC_SK_BACKWARD_MAX_ITERS) return MHC_ERR_ITERS;
+    if (N == 0) return MHC_OK;
+    const bool logits = flags & MHC_SK_LOGITS;
+    if (g_dtype == MHC_DTYPE_F32 && x_dtype == MHC_DTYPE_F32 && g_stride == 16 && x_stride == 16)
+        return logits ? sk_backward<true>(static_cast<const float*>(d_G), static_cast<const float*>(d_X),
+                                          static_cast<float*>(d_D), N, num_iters, stream)
+                      : sk_backward<false>(static_cast<const float*>(d_G), static_cast<const float*>(d_X),
+                                           static_cast<float*>(d_D), N, num_iters, stream);
+    const int iters = num_iters > 0 ? num_iters : 0;
+    if (logits)
+        sk_backward_typed<true>(d_G, g_stride, g_dtype, d_X, x_stride, x_dtype, d_D, N, iters, stream);
+    else
+        sk_backward_typed<false>(d_G, g_stride, g_dtype, d_X, x_stride, x_dtype, d_D, N, iters, stream);
+    return static_cast<int>(cudaGetLastError());
 }
 
 extern "C" int mhc_sinkhorn_knopp_n4_hres(const float* d_h, int64_t h_stride, const float* d_rms,

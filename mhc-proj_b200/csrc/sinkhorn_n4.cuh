@@ -192,10 +192,12 @@ __device__ __forceinline__ float pot_inv(float x, bool keep)
     return keep ? r : 0.0f;
 }
 
-// The forward in potential form: the first iteration's row masks, u_K and
-// v_K, and v_1 .. v_kIters in vh[k - 1][tid].
-template <int kIters, int kBlock>
-__device__ __forceinline__ void pot_forward(const Pairs& M, float eps, float4 (*vh)[kBlock], int tid,
+// The forward in potential form, iters >= 1 iterations (at most the rows of
+// vh): the first iteration's row masks, u_K and v_K, and v_1 .. v_iters in
+// vh[k - 1][tid].  (A compile-time count, as the fixed-count kernels pass,
+// folds into the loops.)
+template <int kBlock>
+__device__ __forceinline__ void pot_forward(const Pairs& M, float eps, float4 (*vh)[kBlock], int tid, int iters,
                                             bool mr[4], float u[4], float v[4])
 {
     float s[4], t[4];
@@ -215,7 +217,7 @@ __device__ __forceinline__ void pot_forward(const Pairs& M, float eps, float4 (*
     }
     vh[0][tid] = make_float4(v[0], v[1], v[2], v[3]);
 #pragma unroll 4
-    for (int k = 1; k < kIters; ++k) {
+    for (int k = 1; k < iters; ++k) {
         pot_rows(M, v, s);
 #pragma unroll
         for (int i = 0; i < 4; ++i) u[i] = pot_inv(s[i], mr[i]);
@@ -227,9 +229,10 @@ __device__ __forceinline__ void pot_forward(const Pairs& M, float eps, float4 (*
 }
 
 // dL/dM from G, given pot_forward's masks, u_K, v_K and history.
-template <int kIters, int kBlock>
+template <int kBlock>
 __device__ __forceinline__ void pot_reverse(const Pairs& M, const Pairs& G, const float4 (*vh)[kBlock], int tid,
-                                            const bool mr[4], const float uK[4], const float vK[4], Pairs& dM)
+                                            int iters, const bool mr[4], const float uK[4], const float vK[4],
+                                            Pairs& dM)
 {
     float du[4], dv[4], v[4];
     {
@@ -248,7 +251,7 @@ __device__ __forceinline__ void pot_reverse(const Pairs& M, const Pairs& G, cons
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] = vK[j];
 #pragma unroll 2
-    for (int k = kIters; k >= 1; --k) {
+    for (int k = iters; k >= 1; --k) {
         float vp[4], s[4], u[4], dt[4], ds[4];
         if (k >= 2) {
             const float4 w = vh[k - 2][tid];

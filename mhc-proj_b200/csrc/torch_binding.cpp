@@ -20,7 +20,8 @@
 // a no-op, and a failed launch raises RuntimeError.  The Newton pair reads
 // fp32/bf16/fp16 CUDA batches with contiguous 4 x 4 matrices in place, at any
 // batch stride, instead of copying them to contiguous fp32 and back; the
-// results are the same bits.
+// results are the same bits.  So do the Sinkhorn-Knopp functions (other
+// layouts of those types are made contiguous in their own type first).
 #include <stdexcept>
 #include <string>
 
@@ -76,6 +77,45 @@ int dtype_code(const torch::Tensor& x)
 bool native_batch(const torch::Tensor& x)
 {
     return x.is_cuda() && dtype_code(x) >= 0 && x.stride(2) == 1 && x.stride(1) == 4 && x.stride(0) >= 0;
+}
+
+// The Sinkhorn-Knopp functions read CUDA fp32/bf16/fp16 batches in their own
+// type: in place at any batch stride when the 4 x 4 matrices are contiguous,
+// else after a copy to contiguous in the same type.  (Converting bf16 logits
+// to fp32 first would take exp of the widened values without the rounding to
+// bf16 that torch.exp in bf16 -- the reference module's -- performs.)
+bool sk_typed(const torch::Tensor& x) { return x.is_cuda() && dtype_code(x) >= 0; }
+
+torch::Tensor sk_layout(const torch::Tensor& x) { return native_batch(x) ? x : x.contiguous(); }
+
+py::dict sk_forward_typed(torch::Tensor X, int max_iter, int flags, const char* what)
+{
+    const c10::cuda::CUDAGuard guard(X.device());
+    X = sk_layout(X);
+    const int64_t n = X.size(0);
+    torch::Tensor T = torch::empty({n, 4, 4}, X.options().memory_format(at::MemoryFormat::Contiguous));
+    check_status(mhc_sinkhorn_knopp_n4_strided(X.data_ptr(), X.stride(0), T.data_ptr(), dtype_code(X), n, max_iter,
+                                               flags, current_stream()),
+                 what);
+    py::dict out;
+    out["T"] = T;
+    return out;
+}
+
+py::dict sk_backward_typed(torch::Tensor G, torch::Tensor X, int max_iter, int flags, const char* what)
+{
+    const c10::cuda::CUDAGuard guard(G.device());
+    G = sk_layout(G);
+    X = sk_layout(X);
+    const int64_t n = G.size(0);
+    torch::Tensor D = torch::empty({n, 4, 4}, G.options().memory_format(at::MemoryFormat::Contiguous));
+    check_status(mhc_sinkhorn_knopp_n4_backward_strided(G.data_ptr(), G.stride(0), dtype_code(G), X.data_ptr(),
+                                                        X.stride(0), dtype_code(X), D.data_ptr(), n, max_iter, flags,
+                                                        current_stream()),
+                 what);
+    py::dict out;
+    out["D"] = D;
+    return out;
 }
 
 // return_stats=True (an optional keyword, ignored-kwargs compatible) adds
@@ -216,6 +256,7 @@ py::dict birkhoff_proj_n4_backward_duals(torch::Tensor G, torch::Tensor R, torch
 py::dict sinkhorn_knopp_n4(torch::Tensor M, int max_iter, const py::kwargs&)
 {
     check_batch(M, "M");
+    if (sk_typed(M)) return sk_forward_typed(M, max_iter, 0, "sinkhorn_knopp_n4");
     const auto src = M.options();
     const auto opts = target_options(M);
     M = M.to(opts);
@@ -237,6 +278,8 @@ py::dict sinkhorn_knopp_n4_backward(torch::Tensor G, torch::Tensor M, int max_it
     if (max_iter > MHC_SK_BACKWARD_MAX_ITERS)
         throw std::invalid_argument("sinkhorn_knopp_n4_backward supports max_iter <= " +
                                     std::to_string(MHC_SK_BACKWARD_MAX_ITERS));
+    if (sk_typed(G) && sk_typed(M) && G.device() == M.device())
+        return sk_backward_typed(G, M, max_iter, 0, "sinkhorn_knopp_n4_backward");
     const auto src = G.options();
     const auto opts = target_options(G);
     G = G.to(opts);
@@ -262,6 +305,9 @@ py::dict sinkhorn_knopp_n4_logits(torch::Tensor R, int max_iter, const py::kwarg
 {
     const bool approx = kwargs.contains("approx_reciprocal") && py::cast<bool>(kwargs["approx_reciprocal"]);
     check_batch(R, "R");
+    if (sk_typed(R))
+        return sk_forward_typed(R, max_iter, MHC_SK_LOGITS | (approx ? MHC_SK_HW_RECIPROCAL : 0),
+                                "sinkhorn_knopp_n4_logits");
     const auto src = R.options();
     const auto opts = target_options(R);
     R = R.to(opts);
@@ -284,6 +330,8 @@ py::dict sinkhorn_knopp_n4_logits_backward(torch::Tensor G, torch::Tensor R, int
     if (max_iter > MHC_SK_BACKWARD_MAX_ITERS)
         throw std::invalid_argument("sinkhorn_knopp_n4_logits_backward supports max_iter <= " +
                                     std::to_string(MHC_SK_BACKWARD_MAX_ITERS));
+    if (sk_typed(G) && sk_typed(R) && G.device() == R.device())
+        return sk_backward_typed(G, R, max_iter, MHC_SK_LOGITS, "sinkhorn_knopp_n4_logits_backward");
     const auto src = G.options();
     const auto opts = target_options(G);
     G = G.to(opts);

@@ -27,6 +27,8 @@ EXPORTED = (
     "mhc_sinkhorn_knopp_n4_logits",
     "mhc_sinkhorn_knopp_n4_logits_ex",
     "mhc_sinkhorn_knopp_n4_logits_backward",
+    "mhc_sinkhorn_knopp_n4_strided",
+    "mhc_sinkhorn_knopp_n4_backward_strided",
     "mhc_birkhoff_proj_n4_hres",
     "mhc_birkhoff_proj_n4_hres_backward_workspace",
     "mhc_birkhoff_proj_n4_hres_backward",
@@ -46,6 +48,7 @@ MHC_ERR_CAPTURE = -3
 MHC_SK_BACKWARD_MAX_ITERS = 20
 MHC_DTYPE_F32, MHC_DTYPE_BF16, MHC_DTYPE_F16 = 0, 1, 2
 MHC_SK_HW_RECIPROCAL = 1
+MHC_SK_LOGITS = 2
 
 
 class MhcError(RuntimeError):
@@ -77,6 +80,8 @@ def lib() -> ctypes.CDLL:
         L.mhc_sinkhorn_knopp_n4_logits.argtypes = [vp, vp, i64, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_ex.argtypes = [vp, vp, i64, i32, i32, vp]
         L.mhc_sinkhorn_knopp_n4_logits_backward.argtypes = [vp, vp, vp, i64, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_strided.argtypes = [vp, i64, vp, i32, i64, i32, i32, vp]
+        L.mhc_sinkhorn_knopp_n4_backward_strided.argtypes = [vp, i64, i32, vp, i64, i32, vp, i64, i32, i32, vp]
         L.mhc_birkhoff_proj_n4_hres.argtypes = [vp, i64, vp, vp, vp, vp, f32, i64, vp]
         L.mhc_birkhoff_proj_n4_hres_backward_workspace.argtypes = [i64, ctypes.POINTER(i64)]
         L.mhc_birkhoff_proj_n4_hres_backward.argtypes = [vp, vp, vp, i64, vp, vp, vp, i64, vp, vp, vp, i64, vp,
@@ -165,6 +170,19 @@ def sinkhorn_knopp_n4_logits_ex(R: int, T: int, N: int, num_iters: int, flags: i
 def sinkhorn_knopp_n4_logits_backward(G: int, R: int, D: int, N: int, num_iters: int, stream: int = 0) -> None:
     _check(lib().mhc_sinkhorn_knopp_n4_logits_backward(G, R, D, N, num_iters, stream),
            "mhc_sinkhorn_knopp_n4_logits_backward")
+
+
+def sinkhorn_knopp_n4_strided(X: int, x_stride: int, T: int, dtype: int, N: int, num_iters: int, flags: int,
+                              stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_strided(X, x_stride, T, dtype, N, num_iters, flags, stream),
+           "mhc_sinkhorn_knopp_n4_strided")
+
+
+def sinkhorn_knopp_n4_backward_strided(G: int, g_stride: int, g_dtype: int, X: int, x_stride: int, x_dtype: int,
+                                       D: int, N: int, num_iters: int, flags: int, stream: int = 0) -> None:
+    _check(lib().mhc_sinkhorn_knopp_n4_backward_strided(G, g_stride, g_dtype, X, x_stride, x_dtype, D, N, num_iters,
+                                                        flags, stream),
+           "mhc_sinkhorn_knopp_n4_backward_strided")
 
 
 def birkhoff_proj_n4_hres(h: int, h_stride: int, rms: int, alpha: int, b: int, T: int, tol: float, N: int,
@@ -362,6 +380,30 @@ def birkhoff_proj_n4_backward_ex_tensor(G, T):
     tp, ts, td = _strided(T, "T")
     D = torch.empty(G.shape, dtype=G.dtype, device=G.device)
     birkhoff_proj_n4_backward_ex(gp, gs, gd, tp, ts, td, D.data_ptr(), G.shape[0], _stream(G))
+    return D
+
+
+def sinkhorn_knopp_n4_strided_tensor(X, num_iters: int = 20, logits: bool = False, approx_reciprocal: bool = False):
+    """Sinkhorn-Knopp (logits=True: on exp(X)) of a strided fp32/bf16/fp16
+    batch; T contiguous in X's dtype."""
+    import torch
+
+    ptr, stride, dt = _strided(X, "X")
+    T = torch.empty(X.shape, dtype=X.dtype, device=X.device)
+    flags = (MHC_SK_LOGITS if logits else 0) | (MHC_SK_HW_RECIPROCAL if approx_reciprocal else 0)
+    sinkhorn_knopp_n4_strided(ptr, stride, T.data_ptr(), dt, X.shape[0], num_iters, flags, _stream(X))
+    return T
+
+
+def sinkhorn_knopp_n4_backward_strided_tensor(G, X, num_iters: int = 20, logits: bool = False):
+    """Its backward on strided batches; D contiguous in G's dtype."""
+    import torch
+
+    gp, gs, gd = _strided(G, "G")
+    xp, xs, xd = _strided(X, "X")
+    D = torch.empty(G.shape, dtype=G.dtype, device=G.device)
+    sinkhorn_knopp_n4_backward_strided(gp, gs, gd, xp, xs, xd, D.data_ptr(), G.shape[0], num_iters,
+                                       MHC_SK_LOGITS if logits else 0, _stream(G))
     return D
 
 

@@ -81,7 +81,10 @@ class MHCSinkhornN4Function(torch.autograd.Function):
         in_shape = R.shape
         R3 = R.reshape(-1, 4, 4)
         ctx.max_iter = max_iter
-        ctx.fused = R3.is_cuda and R3.dtype == torch.float32
+        # CUDA fp32/bf16/fp16: the kernels form exp(R) (rounded to R's type, as
+        # torch.exp in that type) and, backward, the product with it; other
+        # inputs take the reference's composition.
+        ctx.fused = R3.is_cuda and R3.dtype in (torch.float32, torch.bfloat16, torch.float16)
         if ctx.fused:
             T = _internal.torch.sinkhorn_knopp_n4_logits(R3, max_iter, approx_reciprocal=approx_reciprocal)["T"]
             ctx.save_for_backward(R3)

@@ -84,6 +84,36 @@ def test_ex_invalid_arguments_rejected(fn, args):
 
 
 @pytest.mark.parametrize("fn,args", [
+    (capi.sinkhorn_knopp_n4_strided, (FAKE, 16, FAKE, capi.MHC_DTYPE_F32, -1, 20, 0)),
+    (capi.sinkhorn_knopp_n4_strided, (FAKE, -16, FAKE, capi.MHC_DTYPE_F32, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_strided, (FAKE, 16, FAKE, 9, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_strided, (FAKE, 16, 0, capi.MHC_DTYPE_BF16, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_strided, (FAKE, 16, FAKE, capi.MHC_DTYPE_F16, 5, 20, 4)),
+    (capi.sinkhorn_knopp_n4_backward_strided, (FAKE, 16, 5, FAKE, 16, 0, FAKE, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_backward_strided, (FAKE, 16, 0, FAKE, 16, -1, FAKE, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_backward_strided, (FAKE, -1, 0, FAKE, 16, 0, FAKE, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_backward_strided, (FAKE, 16, 0, 0, 16, 0, FAKE, 5, 20, 0)),
+    (capi.sinkhorn_knopp_n4_backward_strided, (FAKE, 16, 0, FAKE, 16, 0, FAKE, 5, 20, capi.MHC_SK_HW_RECIPROCAL)),
+])
+def test_strided_sinkhorn_invalid_arguments_rejected(fn, args):
+    with pytest.raises(capi.MhcError) as e:
+        fn(*args)
+    assert e.value.code == capi.MHC_ERR_INVALID_VALUE
+
+
+def test_strided_sinkhorn_backward_iteration_limit():
+    with pytest.raises(capi.MhcError) as e:
+        capi.sinkhorn_knopp_n4_backward_strided(FAKE, 16, 1, FAKE, 16, 1, FAKE, 5,
+                                                capi.MHC_SK_BACKWARD_MAX_ITERS + 1, capi.MHC_SK_LOGITS)
+    assert e.value.code == capi.MHC_ERR_ITERS
+
+
+def test_strided_sinkhorn_empty_batch_is_a_no_op():
+    capi.sinkhorn_knopp_n4_strided(0, 16, 0, capi.MHC_DTYPE_BF16, 0, 20, capi.MHC_SK_LOGITS)
+    capi.sinkhorn_knopp_n4_backward_strided(0, 16, 1, 0, 16, 2, 0, 0, 20, capi.MHC_SK_LOGITS)
+
+
+@pytest.mark.parametrize("fn,args", [
     (capi.birkhoff_proj_n4_hres, (FAKE, 24, FAKE, FAKE, FAKE, FAKE, 1e-6, -1)),
     (capi.birkhoff_proj_n4_hres, (FAKE, -24, FAKE, FAKE, FAKE, FAKE, 1e-6, 5)),
     (capi.birkhoff_proj_n4_hres, (FAKE, 24, 0, FAKE, FAKE, FAKE, 1e-6, 5)),

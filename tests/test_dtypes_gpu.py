@@ -1,4 +1,5 @@
-"""Native storage types and strided batches for the Newton pair.
+"""Native storage types and strided batches for the Newton and Sinkhorn-Knopp
+pairs.
 
 The reference's wrappers convert every input to contiguous fp32 and the
 outputs back to the input dtype (solvers_torch.cpp:61,67,82,128-136,152).
@@ -88,3 +89,90 @@ def test_module_on_a_bf16_slice_with_autograd():
     assert same_bits(T.detach(), T_conv)
     D_conv = capi.birkhoff_proj_n4_backward_tensor(G.float().contiguous(), T_conv.float()).to(torch.bfloat16)
     assert same_bits(x.grad, D_conv)
+
+
+# ---- the Sinkhorn-Knopp pair -------------------------------------------------
+#
+# The reference's SK wrappers convert to contiguous fp32 and back
+# (solvers_torch.cpp:190,196,211,258-266,282) and its MHCSinkhornN4 computes
+# torch.exp, and the final D * expon, in the input's type (module.py:50,70).
+# The kernels here read and write the native type in place; the expected
+# values below are that composition, on this repository's fp32 kernels (which
+# are bitwise the reference's for the forward; the backward is the exact VJP).
+
+def sk_reference_forward(X, iters, logits):
+    M = torch.exp(X) if logits else X
+    return capi.sinkhorn_knopp_n4_tensor(M.float().contiguous(), iters).to(X.dtype)
+
+
+def sk_reference_backward(G, X, iters, logits):
+    M = torch.exp(X) if logits else X
+    D = capi.sinkhorn_knopp_n4_backward_tensor(G.float().contiguous(), M.float().contiguous(), iters).to(G.dtype)
+    return D * M if logits else D
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("stride,offset", [(16, 0), (24, 8), (20, 4), (16, 1)])
+@pytest.mark.parametrize("logits", [False, True])
+def test_sinkhorn_forward_native_equals_reference_composition(dtype, stride, offset, logits):
+    n = 30001
+    X = strided_batch("sigma_mix", n, dtype, stride, offset, seed=40 + stride + offset)
+    if not logits:
+        X.copy_(torch.exp(X.float()).to(dtype))
+    for iters in (0, 1, 20):
+        fn = mhc_proj.torch.sinkhorn_knopp_n4_logits if logits else mhc_proj.torch.sinkhorn_knopp_n4
+        T = fn(X, iters)["T"]
+        assert T.dtype == dtype and T.is_contiguous()
+        expected = sk_reference_forward(X, iters, logits)
+        assert same_bits(T, expected), (iters, logits)
+        assert same_bits(capi.sinkhorn_knopp_n4_strided_tensor(X, iters, logits=logits), expected)
+
+
+@pytest.mark.parametrize("gdt", DTYPES)
+@pytest.mark.parametrize("xdt", DTYPES)
+@pytest.mark.parametrize("logits", [False, True])
+def test_sinkhorn_backward_native_equals_reference_composition(gdt, xdt, logits):
+    """D in G's type.  With logits the composition's product is in the
+    promoted type when G's and R's types differ; the fused backward rounds it
+    to G's type (the module always passes G and R of the same type)."""
+    n = 20000
+    X = strided_batch("normal", n, xdt, 24, 8, seed=11)
+    if not logits:
+        X.copy_(torch.exp(X.float()).to(xdt))
+    G = strided_batch("normal", n, gdt, 20, 4, seed=12)
+    for iters in (0, 1, 7, 20):
+        fn = mhc_proj.torch.sinkhorn_knopp_n4_logits_backward if logits else mhc_proj.torch.sinkhorn_knopp_n4_backward
+        D = fn(G, X, iters)["D"]
+        assert D.dtype == gdt and D.is_contiguous()
+        expected = sk_reference_backward(G, X, iters, logits).to(gdt)
+        assert same_bits(D, expected), (iters, logits)
+        assert same_bits(capi.sinkhorn_knopp_n4_backward_strided_tensor(G, X, iters, logits=logits), expected)
+
+
+def test_sinkhorn_native_paths_reach_both_kernels_layouts():
+    """A non-native layout of a native type (a transposed batch) is made
+    contiguous in its own type: the same bits as the contiguous input."""
+    n = 4099
+    X = make_logits("normal", n, seed=21).to(torch.bfloat16)
+    Xt = X.transpose(1, 2).contiguous().transpose(1, 2)  # the same values, column-major matrices
+    assert not Xt.is_contiguous()
+    assert same_bits(mhc_proj.torch.sinkhorn_knopp_n4_logits(Xt, 20)["T"],
+                     mhc_proj.torch.sinkhorn_knopp_n4_logits(X, 20)["T"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_sinkhorn_module_on_a_slice_with_autograd(dtype):
+    """MHCSinkhornN4 on H_res logits as the mHC layer holds them: columns
+    8..23 of a (tokens, 24) projection output in bf16/fp16, read in place;
+    T and the input gradient are the reference module's bits."""
+    n = 8192
+    H = make_logits("normal", n * 24 // 16, seed=31).reshape(n, 24).to(dtype)
+    x = H[:, 8:24].reshape(n, 4, 4)
+    assert x.stride(0) == 24
+    xa = H.clone().requires_grad_(True)
+    T = mhc_proj.MHCSinkhornN4(max_iter=20)(xa[:, 8:24].reshape(n, 4, 4))
+    G = make_logits("normal", n, seed=32).to(dtype)
+    (T * G).sum().backward()
+    assert same_bits(T.detach(), sk_reference_forward(x, 20, True))
+    assert same_bits(xa.grad[:, 8:24].reshape(n, 4, 4), sk_reference_backward(G, x, 20, True))
+    assert bool((xa.grad[:, :8] == 0).all())
