@@ -301,6 +301,37 @@ def test_fuzz_against_reference(ref, R, G, tol):
     assert bitwise_equal(capi.birkhoff_proj_n4_backward_tensor(Gd, Tr), ref_backward(ref, Gd, Tr))
 
 
+@settings(max_examples=40, deadline=None)
+@given(scale=st.floats(0.05, 12.0), shift=st.floats(-30.0, 5.0), iters=st.integers(1, 20),
+       seed=st.integers(0, 2**31 - 1), masked=st.booleans())
+def test_fuzz_sinkhorn_backward_against_oracle(scale, shift, iters, seed, masked):
+    """The SK backward (from the forward's potentials, the first iteration's
+    masks) against the oracle's step-by-step exact VJP on random scales of
+    the logits (up to N(0, 144)), shifts that push whole matrices towards eps,
+    random iteration counts and, optionally, rows and columns of -40 planted
+    in.  dR = dM * M, what a caller uses, within 2e-6; rows whose sum is at
+    most eps exactly zero on both sides; dM itself within 2e-6 relative where
+    M > 1e-6 on well-conditioned draws (on ill-conditioned ones dM = dR / M
+    carries each form's rounding, amplified, in both)."""
+    n = 256
+    g = torch.Generator().manual_seed(seed)
+    R = torch.randn(n, 4, 4, generator=g) * scale + shift
+    if masked:
+        R[::5, 1, :] = -40.0
+        R[2::7, :, 2] = -40.0
+    G = torch.randn(n, 4, 4, generator=g)
+    M = torch.exp(R)
+    D = capi.sinkhorn_knopp_n4_backward_tensor(G.cuda(), M.cuda(), iters).cpu().numpy()
+    Mn = M.numpy()
+    Do = oracle.sinkhorn_knopp_n4_backward(G.numpy(), Mn, iters, 1e-8, exact=True)
+    assert (np.abs(D * Mn - Do * Mn) <= 2e-6).all()
+    rows = Mn.sum(2) <= 1e-8
+    assert (D[rows] == 0).all() and (Do[rows] == 0).all()
+    if scale <= 1.0 and shift >= -5.0:
+        big = Mn > 1e-6
+        assert (np.abs(D - Do)[big] <= 2e-6 * np.maximum(1.0, np.abs(Do[big]))).all()
+
+
 def test_batch_beyond_int32_element_indexing():
     """N = 2^27 + 5 matrices (2^31 + 80 elements per tensor): past the point
     where the reference's 32-bit element index N*16 overflows
