@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--dist", default="normal", choices=["normal", "sigma_mix", "mixture", "wide"])
     ap.add_argument("--tol", type=float, default=1e-6)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-chunks", type=int, default=16, help="pieces of the e2e step's batch (pipelined copies)")
+    ap.add_argument("--e2e-streams", type=int, default=3, help="streams the e2e pieces rotate over")
     ap.add_argument("--mixture-total", type=int, default=1 << 26,
                     help="matrices of the sharded mixture measurement (total over all ranks; 0 skips it)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
@@ -815,12 +817,12 @@ def run_e2e(args, R, G, dev, world):
     import mhc_proj
 
     n = R.shape[0]
-    chunks = 16 if n >= (1 << 20) else 1
+    chunks = args.e2e_chunks if n >= (1 << 20) else 1
     Rh = R.cpu().pin_memory()
     Gh = G.cpu().pin_memory()
     Th = torch.empty_like(Rh).pin_memory()
     Dh = torch.empty_like(Rh).pin_memory()
-    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
+    streams = [torch.cuda.Stream(device=dev) for _ in range(max(1, args.e2e_streams))]
     bounds = [(n * i // chunks, n * (i + 1) // chunks) for i in range(chunks)]
     tol = args.tol
 
