@@ -332,6 +332,30 @@ def test_fuzz_sinkhorn_backward_against_oracle(scale, shift, iters, seed, masked
         assert (np.abs(D - Do)[big] <= 2e-6 * np.maximum(1.0, np.abs(Do[big]))).all()
 
 
+def test_sinkhorn_batch_beyond_int32_element_indexing():
+    """The fused Sinkhorn-Knopp pair on N = 2^27 + 5 matrices (2^31 + 80
+    elements per tensor): slices at both ends and across the 2^31-element
+    boundary equal separate launches on those slices, bit for bit."""
+    n = (1 << 27) + 5
+    free, _ = torch.cuda.mem_get_info()
+    if free < 5 * n * 64:
+        pytest.skip("needs ~45 GB of free device memory")
+    R = torch.empty(n, 4, 4, device="cuda")
+    for i in range(0, n, 1 << 24):
+        m = min(1 << 24, n - i)
+        R[i:i + m] = make_logits("normal", m, seed=91 + i // (1 << 24))
+    G = torch.empty_like(R).normal_()
+    T = capi.sinkhorn_knopp_n4_logits_tensor(R, 20)
+    D = capi.sinkhorn_knopp_n4_logits_backward_tensor(G, R, 20)
+    edge = (1 << 27) - 1000
+    for a, b in [(0, 4096), (edge, edge + 2000), (n - 3000, n)]:
+        assert bitwise_equal(T[a:b], capi.sinkhorn_knopp_n4_logits_tensor(R[a:b].contiguous(), 20))
+        assert bitwise_equal(D[a:b], capi.sinkhorn_knopp_n4_logits_backward_tensor(G[a:b].contiguous(),
+                                                                                   R[a:b].contiguous(), 20))
+    del R, G, T, D
+    torch.cuda.empty_cache()
+
+
 def test_batch_beyond_int32_element_indexing():
     """N = 2^27 + 5 matrices (2^31 + 80 elements per tensor): past the point
     where the reference's 32-bit element index N*16 overflows
