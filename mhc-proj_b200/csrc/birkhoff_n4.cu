@@ -276,11 +276,14 @@ __global__ void __launch_bounds__(32 * kWarps, 1) birkhoff_fwd_kernel(Src src, E
     // kStats with counts: the warp's pass counts, the same in every lane
     unsigned tally[MHC_PASS_COUNTERS] = {};
 
+    // gamma_k of the next step, loaded where k is updated (ahead of the
+    // step that uses it)
+    float gamma_next = gtab[k];
     while (__any_sync(kFullMask, stage != kIdle)) {
         const bool s_start = stage == kStart, s_cand = stage == kCand;
         const bool s_skcol = stage == kSkCol, s_skeval = stage == kSkEval;
 
-        const float gamma = gtab[k];
+        const float gamma = gamma_next;
         // Point of evaluation (rows) or per-row offsets (columns).
         float v[4];
 #pragma unroll
@@ -362,6 +365,7 @@ __global__ void __launch_bounds__(32 * kWarps, 1) birkhoff_fwd_kernel(Src src, E
             for (int j = 0; j < 4; ++j) d[j] = sel(next_iter, dn[j], d[j]);
         }
         k = sel(next_iter, 0, sel(s_cand && !accept, k + 1, k));
+        gamma_next = gtab[k];
         stage = sel(stage == kIdle || done, static_cast<int>(kIdle),
                 sel(next_iter, static_cast<int>(kCand),
                 sel(reject_last, static_cast<int>(kSkCol),
