@@ -86,7 +86,7 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_forward_counts(kernel="forward"):
+def ncu_counts(kernel="forward"):
     """Per-matrix DRAM bytes, warp instructions and MUFU operations of a
     kernel ("forward", "sk_backward", ...) from the committed ncu summary
     (profiles/roofline_traffic.json), or Nones."""
@@ -401,7 +401,7 @@ def run_ours(args):
         fwd_gbs = BYTES_FWD * n / (fwd_ms * 1e-3) / 1e9
         bwd_gbs = BYTES_BWD * n / (bwd_ms * 1e-3) / 1e9
         step_gbs = (BYTES_FWD + BYTES_BWD) * n / (ms_per_step * 1e-3) / 1e9
-        tpm, wipm, mufupm = ncu_forward_counts()
+        tpm, wipm, mufupm = ncu_counts()
         sms = sm_count(dev)
         clocks = clk.summary()
         mhz = clocks["sm_mhz"] if clocks else 1965.0
@@ -468,7 +468,7 @@ def run_ours(args):
         if args.workload == "sinkhorn":
             # the backward is the dominant kernel of this step
             line["metric"] = "Sinkhorn-Knopp n4 (20 iterations) fwd+bwd matrices/s"
-            btpm, bwipm, _ = ncu_forward_counts("sk_backward")
+            btpm, bwipm, _ = ncu_counts("sk_backward")
             rate_bwd = n / (bwd_ms * 1e-3)
             line["roofline"].update({
                 "kernel": "sk_bwd_kernel (fused exp; exact VJP from the forward's potentials)",
@@ -518,7 +518,7 @@ def run_ours(args):
             bwd_gbs = BYTES_SKHRES_BWD * n / (bwd_ms * 1e-3) / 1e9
             step_gbs = (BYTES_HRES_FWD + BYTES_SKHRES_BWD) * n / (ms_per_step * 1e-3) / 1e9
             line["metric"] = "H_res producer + Sinkhorn-Knopp n4 (20 iterations) fwd+bwd matrices/s"
-            btpm, bwipm, _ = ncu_forward_counts("sk_hres_backward")
+            btpm, bwipm, _ = ncu_counts("sk_hres_backward")
             rate_bwd = n / (bwd_ms * 1e-3)
             line["roofline"].update({
                 "kernel": "sk_hres_bwd_kernel (the dominant kernel: the producer's chain rule fused into the "
